@@ -1,0 +1,44 @@
+// common.cuh — shared definitions for the B200 attention library (internal).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gpt2_b200.h"
+
+namespace b200 {
+
+// Device status-word bits. Kernels OR these into a per-device word instead of trapping; the host
+// reads them with gpt2_b200_status().
+enum StatusBits : unsigned {
+    ST_PREFILL_LOAD_TIMEOUT = 1u << 0,     // TMA producer gave up waiting for a free stage
+    ST_PREFILL_MMA_TIMEOUT = 1u << 1,      // MMA issuer gave up waiting for data / softmax
+    ST_PREFILL_SOFTMAX_TIMEOUT = 1u << 2,  // softmax warps gave up waiting for the MMA
+    ST_PREFILL_SMEM_ALIGN = 1u << 3,       // dynamic shared memory not 1024-byte aligned
+    ST_PREFILL_DRAIN_TIMEOUT = 1u << 4,    // teardown could not confirm in-flight copies / MMAs
+    ST_DECODE_BAD_LEN = 1u << 8,           // device-side length outside [1, maxT]
+    ST_KV_BAD_POS = 1u << 9,               // device-side append position outside [0, maxT)
+    ST_TEST_WAIT_TIMEOUT = 1u << 16,       // the wait-timeout self-test expired (expected)
+};
+
+// Default bound on any single mbarrier wait inside a kernel (wall clock). A correct kernel waits
+// microseconds; the bound only matters when something is broken.
+constexpr unsigned long long kDefaultWaitTimeoutNs = 2000000000ull;
+
+struct DeviceContext {
+    unsigned *status = nullptr;     // one word, zero = healthy
+    float *part = nullptr;          // decode split partials
+    unsigned *counters = nullptr;   // decode split-arrival counters (kept at zero between calls)
+    size_t part_floats = 0;
+    size_t counter_words = 0;
+    bool prefill_attr_done = false;
+    int num_sms = 0;
+};
+
+// Returns the context of the current device (creating it on first use), or nullptr on CUDA error.
+DeviceContext *device_context();
+unsigned long long wait_timeout_ns();
+void set_last_error(int code);
+
+}  // namespace b200

@@ -1,0 +1,189 @@
+/* gpt2_b200.h — C ABI of the B200 (sm_100a) causal self-attention library for GPT-2-124M.
+ *
+ * Drop-in replacements for the attention hot path of MatteoPhan926/bare-metal-gpt2:
+ *   prefill : the GPT2Backend.attention slot          (cuda/kernels.cuh:73), implemented by
+ *             gpt2_attention_flash in the reference   (cuda/kernels_fused.cu:145-149);
+ *   decode  : gpt2_attn_decode over the KV cache      (cuda/kvcache.cuh:54, cuda/kvcache.cu:207-210);
+ *   cache   : the GPT2KVCache arena, its alloc/free/reset/step-bytes helpers and the append / prefill
+ *             scatter writers (cuda/kvcache.cuh:39-66, cuda/kvcache.cu:25-81,204-206).
+ *
+ * Conventions (same as the reference unless stated):
+ *   - fp16 storage, fp32 accumulation; qkv rows are [q(E) | k(E) | v(E)], head h at h*D in each part;
+ *     att rows are E wide. Causal: query i attends keys 0..i; scale 1/sqrt(D).
+ *   - The cache layout is the reference's: per layer L, K at data + (2L)*H*maxT*D and V at
+ *     data + (2L+1)*H*maxT*D, each [head][pos][dim] (cuda/kvcache.cuh:31-33,61-66).
+ *   - All pointers are device pointers unless a parameter says "host". The caller owns every buffer.
+ *   - The reference-signature entry points return void and launch on the legacy default stream, as the
+ *     reference does; their argument / launch errors are kept in a per-thread "last error"
+ *     (gpt2_b200_last_error). The _stream / _status variants return a GPT2_B200_* code.
+ *   - Kernels never trap or spin forever: every wait is bounded, and a timeout sets a bit in a
+ *     per-device status word read by gpt2_b200_status().
+ *   - Shapes: D must be 64 (the reference's flash kernel has the same restriction, kernels_fused.cu:56);
+ *     E = H*64; 16-byte aligned qkv / att / cache pointers.
+ */
+#ifndef GPT2_B200_H
+#define GPT2_B200_H
+
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+#include <cuda_fp16.h>
+typedef __half gpt2_half; /* the reference's `half` */
+extern "C" {
+#else
+typedef struct { unsigned short bits; } gpt2_half;
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define GPT2_B200_OK 0
+#define GPT2_B200_EINVAL 1      /* bad argument (shape, alignment, length, null pointer) */
+#define GPT2_B200_ECUDA 2       /* a CUDA runtime call failed */
+#define GPT2_B200_ENOMEM 3      /* allocation refused (cache plan over budget, workspace) */
+#define GPT2_B200_EDEVICE 4     /* the device is not an sm_100 part, or the driver lacks TMA */
+#define GPT2_B200_ETIMEOUT 5    /* a kernel's bounded wait expired (see gpt2_b200_status) */
+#define GPT2_B200_ECAPTURE 6    /* would need to allocate while the stream is being captured */
+
+/* ---------------------------------------------------------------- the KV cache (reference ABI)
+ * Identical layout to GPT2KVCache in cuda/kvcache.cuh:39-44. If the reference's kvcache.cuh is
+ * included first, its definition is used (include the reference headers before this one). */
+#ifndef GPT2_KVCACHE_CUH
+typedef struct GPT2KVCache {
+    gpt2_half *data; /* owns the whole arena (device) */
+    size_t bytes;
+    int maxT, nLayer, nHead, headDim;
+    int len;         /* positions currently cached [0, len) */
+} GPT2KVCache;
+#endif
+
+/* ---------------------------------------------------------------- the backend table (reference ABI)
+ * Identical layout to GPT2Backend in cuda/kernels.cuh:68-86 (opaque function pointers here, so this
+ * header does not need the reference's weight types). */
+#ifndef GPT2_KERNELS_CUH
+typedef struct {
+    const char *name;
+    void (*embed)(void);
+    void (*layernorm)(void);
+    void (*matmul)(void);
+    void (*attention)(gpt2_half *att, const gpt2_half *qkv, int T, int E, int H, int D);
+    void (*gelu)(void);
+    void (*add)(void);
+    void (*matmul_q)(void);
+    void (*gemv)(void);
+    void (*gemv_q)(void);
+} GPT2Backend;
+#endif
+
+/* ================================================================ prefill attention */
+
+/* Replaces GPT2Backend.attention / gpt2_attention_flash (cuda/kernels.cuh:73,
+ * cuda/kernels_fused.cu:145-149): att[T,E] = causal softmax(q k^T / sqrt(D)) v for every head of
+ * qkv[T,3E]. Same signature and semantics; runs the tcgen05/TMEM tensor-core kernel on the legacy
+ * default stream. */
+void gpt2_attention_b200(gpt2_half *att, const gpt2_half *qkv, int T, int E, int H, int D);
+
+/* Stream variant of gpt2_attention_b200 (additive extension; no reference counterpart). */
+int gpt2_attention_b200_stream(gpt2_half *att, const gpt2_half *qkv, int T, int E, int H, int D,
+                               cudaStream_t stream);
+
+/* Batched prefill: B independent sequences (or layers) in one launch. Sequence b reads
+ * qkv + b*qkv_seq_stride and writes att + b*att_seq_stride (strides in elements; 0 = dense,
+ * i.e. T*3E and T*E). Additive extension of cuda/kernels.cuh:73 for batch > 1. */
+int gpt2_attention_b200_batched(gpt2_half *att, const gpt2_half *qkv, int B, int T, int E, int H,
+                                int D, long long qkv_seq_stride, long long att_seq_stride,
+                                cudaStream_t stream);
+
+/* ================================================================ decode attention */
+
+/* Replaces gpt2_attn_decode (cuda/kvcache.cuh:54, cuda/kvcache.cu:207-210): M=1 attention of the
+ * step's query (the first E halves of qkv) over keys 0..len-1 of layer L of the cache; writes att[E].
+ * Split-context flash-decoding with an in-kernel combine. Legacy default stream. */
+void gpt2_attn_decode_b200(gpt2_half *att, const gpt2_half *qkv, const GPT2KVCache *kv, int L,
+                           int len);
+
+/* Stream variant (additive extension). */
+int gpt2_attn_decode_b200_stream(gpt2_half *att, const gpt2_half *qkv, const GPT2KVCache *kv,
+                                 int L, int len, cudaStream_t stream);
+
+/* Decode attention for layers L0 .. L0+nL-1 of one cache in ONE launch. Layer l (relative) reads its
+ * query at q + l*q_layer_stride and writes att + l*att_layer_stride (elements). The key count is
+ * *d_len when d_len is not NULL (a device int, so a captured CUDA graph replays with a growing
+ * context), else len. max_len bounds the split count (0 = kv->maxT). Additive extension. */
+int gpt2_attn_decode_b200_layers(gpt2_half *att, long long att_layer_stride, const gpt2_half *q,
+                                 long long q_layer_stride, const GPT2KVCache *kv, int L0, int nL,
+                                 const int *d_len, int len, int max_len, cudaStream_t stream);
+
+/* Decode attention for B independent sequences, one layer each, in ONE launch: sequence b attends
+ * over the [H][maxT][D] K and V slabs at k_slabs[b] / v_slabs[b] (device arrays of device pointers)
+ * for d_lens[b] keys (device ints), query q + b*q_stride, output att + b*att_stride. max_len bounds
+ * the split count. Additive extension (batched decode over a [B] array of caches). */
+int gpt2_attn_decode_b200_batched(gpt2_half *att, long long att_stride, const gpt2_half *q,
+                                  long long q_stride, const gpt2_half *const *k_slabs,
+                                  const gpt2_half *const *v_slabs, const int *d_lens, int B, int H,
+                                  int maxT, int max_len, cudaStream_t stream);
+
+/* The attention part of one decode step for every layer (the ordering of
+ * gpt2_decode_step_cuda, cuda/kvcache.cu:249-252): append this step's K,V (from qkv rows
+ * qkv + l*qkv_layer_stride) at position pos, then attend over len = pos+1 for all layers.
+ * pos is *d_pos when d_pos is not NULL (graph replay), else the host value. Two launches.
+ * Does not touch kv->len (the reference sets it on the host after the step, kvcache.cu:268). */
+int gpt2_b200_decode_attn_step(gpt2_half *att, long long att_layer_stride, const gpt2_half *qkv,
+                               long long qkv_layer_stride, GPT2KVCache *kv, const int *d_pos,
+                               int pos, cudaStream_t stream);
+
+/* ================================================================ the KV cache */
+
+/* Replaces gpt2_kv_alloc (cuda/kvcache.cu:29-45): one arena of 2*L*H*maxT*D halves for the GPT-2-124M
+ * shape (12 layers, 12 heads, D 64), refused (returns 1) when it would leave < 64 MiB free. 0 = ok. */
+int gpt2_kv_alloc_b200(GPT2KVCache *kv, int maxT);
+/* Same, for an explicit shape (additive extension). */
+int gpt2_kv_alloc_shape_b200(GPT2KVCache *kv, int nLayer, int nHead, int headDim, int maxT);
+/* Replaces gpt2_kv_free / gpt2_kv_reset / gpt2_kv_step_bytes (cuda/kvcache.cu:47-52). */
+void gpt2_kv_free_b200(GPT2KVCache *kv);
+void gpt2_kv_reset_b200(GPT2KVCache *kv);
+double gpt2_kv_step_bytes_b200(const GPT2KVCache *kv, int len);
+
+/* Replaces gpt2_kv_append_one (cuda/kvcache.cu:57-64,204-206): writes the K and V parts of qkv[3E]
+ * into layer L at position pos, 16-byte vector stores. Legacy default stream. */
+void gpt2_kv_append_one_b200(GPT2KVCache *kv, int L, const gpt2_half *qkv, int pos);
+/* Append for layers L0..L0+nL-1 (rows qkv + l*qkv_layer_stride); position *d_pos if d_pos != NULL. */
+int gpt2_kv_append_b200_stream(GPT2KVCache *kv, int L0, int nL, const gpt2_half *qkv,
+                               long long qkv_layer_stride, const int *d_pos, int pos,
+                               cudaStream_t stream);
+
+/* Replaces gpt2_kv_scatter_prefill (cuda/kvcache.cu:67-81): rows 0..T-1 of qkv[T,3E] into layer L,
+ * positions 0..T-1. Legacy default stream. */
+void gpt2_kv_scatter_prefill_b200(GPT2KVCache *kv, int L, const gpt2_half *qkv, int T);
+int gpt2_kv_scatter_prefill_b200_stream(GPT2KVCache *kv, int L, const gpt2_half *qkv, int T,
+                                        cudaStream_t stream);
+
+/* ================================================================ backend, status, set-up */
+
+/* Composes a backend the reference's way (cuda/kernels_fused.cu:157-164): copies *base and installs
+ * gpt2_attention_b200 as .attention and "b200" as .name. base may be NULL (all other slots NULL). */
+void gpt2_b200_compose_backend(GPT2Backend *dst, const GPT2Backend *base);
+
+/* Reserves decode workspace on the current device for `jobs` (layer x sequence) decodes of up to
+ * max_len keys, so that later calls (e.g. inside CUDA graph capture) do not allocate. */
+int gpt2_b200_reserve(int jobs, int n_head, int max_len);
+
+/* Synchronises the current device and returns the device status word (0 = healthy; bits name the
+ * kernel and wait that timed out). clear != 0 resets it. */
+unsigned gpt2_b200_status(int clear);
+
+/* Last argument / launch error of a void entry point on this host thread (GPT2_B200_*); clears it. */
+int gpt2_b200_last_error(void);
+const char *gpt2_b200_strerror(int code);
+
+/* Self-test of the bounded-wait path: launches one CTA that waits on an mbarrier nothing arrives on,
+ * with a timeout of timeout_us microseconds. Returns GPT2_B200_ETIMEOUT when the wait expired and the
+ * kernel returned cleanly (the expected result); the device context stays usable. */
+int gpt2_b200_selftest_wait_timeout(unsigned timeout_us);
+
+/* Library version and the number of kernels each entry point launches (for launch accounting). */
+const char *gpt2_b200_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+#endif /* GPT2_B200_H */

@@ -1,0 +1,122 @@
+"""C ABI surface checks that need no GPU: exports, header validity, struct layouts, host logic and
+argument validation (which happens before any CUDA call)."""
+import ctypes
+import os
+import subprocess
+import tempfile
+
+import pytest
+
+import gpt2_b200 as G
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_exports_every_declared_function(lib):
+    declared = G.header_functions()
+    assert len(declared) >= 20
+    missing = [n for n in declared if not hasattr(lib.lib, n)]
+    assert not missing, f"declared in include/gpt2_b200.h but not exported: {missing}"
+    # and the binding declares a signature for each
+    assert sorted(G._SIGS) == declared
+
+
+def _compile_c_probe(src: str) -> str:
+    d = tempfile.mkdtemp()
+    c = os.path.join(d, "probe.c")
+    exe = os.path.join(d, "probe")
+    open(c, "w").write(src)
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    "-I", "/usr/local/cuda/include", "-o", exe, c], check=True,
+                   capture_output=True)
+    return subprocess.run([exe], check=True, capture_output=True, text=True).stdout
+
+
+def test_header_is_valid_c_and_struct_layouts_match_reference():
+    src = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "gpt2_b200.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu\n", sizeof(GPT2KVCache), offsetof(GPT2KVCache, bytes),
+         offsetof(GPT2KVCache, maxT), offsetof(GPT2KVCache, len), sizeof(GPT2Backend),
+         offsetof(GPT2Backend, attention));
+  return 0;
+}'''
+    vals = [int(x) for x in _compile_c_probe(src).split()]
+    # GPT2KVCache {half*; size_t; int x4; int len} (cuda/kvcache.cuh:39-44) on LP64
+    assert vals[:4] == [40, 8, 16, 32]
+    assert vals[0] == ctypes.sizeof(G.GPT2KVCache)
+    # GPT2Backend: name + 9 function pointers (cuda/kernels.cuh:68-86); .attention is slot 4
+    assert vals[4] == 80 and vals[5] == 32
+    assert vals[4] == ctypes.sizeof(G.GPT2Backend)
+
+
+def test_compose_backend_the_reference_way(lib):
+    base = G.GPT2Backend()
+    base.name = b"gemv"
+    for i, f in enumerate(("embed", "layernorm", "matmul", "attention", "gelu", "add", "matmul_q",
+                           "gemv", "gemv_q")):
+        setattr(base, f, 0x1000 + i)
+    dst = G.GPT2Backend()
+    lib.gpt2_b200_compose_backend(ctypes.byref(dst), ctypes.byref(base))
+    assert dst.name == b"b200"
+    attn_addr = ctypes.cast(lib.lib.gpt2_attention_b200, ctypes.c_void_p).value
+    assert dst.attention == attn_addr
+    assert (dst.embed, dst.matmul, dst.gemv, dst.gemv_q) == (0x1000, 0x1002, 0x1007, 0x1008)
+    empty = G.GPT2Backend()
+    lib.gpt2_b200_compose_backend(ctypes.byref(empty), None)
+    assert empty.attention == attn_addr and empty.matmul is None
+
+
+def test_kv_step_bytes_formula(lib):
+    kv = G.cache_view(0, 12, 1024)
+    for n in (1, 128, 512, 1023):
+        assert lib.gpt2_kv_step_bytes_b200(ctypes.byref(kv), n) == 36864.0 * n
+
+
+@pytest.mark.parametrize("T,E,H,D", [(4, 768, 12, 32), (4, 700, 12, 64), (-1, 768, 12, 64),
+                                     (4, 768, 0, 64)])
+def test_prefill_rejects_bad_shapes(lib, T, E, H, D):
+    assert lib.gpt2_attention_b200_stream(16, 16, T, E, H, D, None) == G.EINVAL
+    lib.gpt2_attention_b200(16, 16, T, E, H, D)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+    assert lib.gpt2_b200_last_error() == G.OK  # reading clears it
+
+
+def test_prefill_rejects_misaligned_pointers(lib):
+    assert lib.gpt2_attention_b200_stream(18, 16, 4, 768, 12, 64, None) == G.EINVAL
+    assert lib.gpt2_attention_b200_stream(16, 0, 4, 768, 12, 64, None) == G.EINVAL
+    assert lib.gpt2_attention_b200_batched(16, 16, 2, 4, 768, 12, 64, 13, 0, None) == G.EINVAL
+
+
+def test_prefill_empty_is_a_no_op(lib):
+    assert lib.gpt2_attention_b200_batched(None, None, 0, 4, 768, 12, 64, 0, 0, None) == G.OK
+    assert lib.gpt2_attention_b200_batched(None, None, 3, 0, 768, 12, 64, 0, 0, None) == G.OK
+
+
+def test_decode_rejects_bad_arguments(lib):
+    kv = G.cache_view(0, 12, 1024)  # data == NULL
+    assert lib.gpt2_attn_decode_b200_stream(16, 16, ctypes.byref(kv), 0, 5, None) == G.EINVAL
+    assert lib.gpt2_attn_decode_b200_stream(16, 16, None, 0, 5, None) == G.EINVAL
+    kv = G.cache_view(4096, 12, 1024)
+    for L, n in ((0, 0), (0, 1025), (-1, 5), (12, 5)):
+        assert lib.gpt2_attn_decode_b200_stream(16, 16, ctypes.byref(kv), L, n, None) == G.EINVAL
+    bad = G.cache_view(4096, 12, 1024, head_dim=32)
+    assert lib.gpt2_attn_decode_b200_stream(16, 16, ctypes.byref(bad), 0, 5, None) == G.EINVAL
+    lib.gpt2_attn_decode_b200(16, 16, ctypes.byref(kv), 0, 0)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+
+
+def test_kv_writers_reject_bad_positions(lib):
+    kv = G.cache_view(4096, 12, 64)
+    assert lib.gpt2_kv_append_b200_stream(ctypes.byref(kv), 0, 1, 16, 0, None, 64, None) == G.EINVAL
+    assert lib.gpt2_kv_append_b200_stream(ctypes.byref(kv), 11, 2, 16, 0, None, 0, None) == G.EINVAL
+    assert lib.gpt2_kv_scatter_prefill_b200_stream(ctypes.byref(kv), 0, 16, 65, None) == G.EINVAL
+    lib.gpt2_kv_append_one_b200(ctypes.byref(kv), 0, 16, -1)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+
+
+def test_strerror_and_version(lib):
+    assert lib.gpt2_b200_strerror(G.ETIMEOUT) == b"a kernel wait timed out"
+    assert b"sm_100a" in lib.gpt2_b200_version()

@@ -1,0 +1,127 @@
+"""Prefill parity on the GPU: the tcgen05 kernel (through the C ABI) against the oracle (the
+reference's cpu/forward_cpu.c attention restated, double precision) and against the reference's own
+k_attention_flash (cuda/kernels_fused.cu:58-149) compiled for sm_100a, on the same seeded fp16 inputs.
+Tolerance: max-abs 2e-3 and max|diff|/max|ref| 1e-2 (conftest.ABS_TOL / REL_TOL)."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+SENTINEL = 12344.0  # exactly representable in fp16
+
+
+def dev16(torch, x):
+    return torch.from_numpy(np.ascontiguousarray(x).astype(np.float16)).cuda()
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+# T values: 1, tile edges (127/128/129, 255/256/257), the reference's odd prompt length 161, 1024.
+@pytest.mark.parametrize("T", [1, 2, 31, 32, 33, 127, 128, 129, 161, 255, 256, 257, 512, 1000, 1024])
+def test_prefill_matches_oracle_and_reference_flash(cuda, lib, oracle, ref_gpu, T):
+    x = O.seeded_qkv(2000 + T, T)
+    qkv = dev16(cuda, x)
+    att = cuda.full((T, O.E), SENTINEL, dtype=cuda.float16, device="cuda")
+    lib.prefill(att, qkv, T)
+    cuda.cuda.synchronize()
+    assert lib.status() == 0
+    got = host(att)
+    assert_close(got, oracle.prefill(x), f"T={T} vs oracle")
+    ref = cuda.empty_like(att)
+    ref_gpu.attention_flash(ref.data_ptr(), qkv.data_ptr(), T)
+    assert_close(got, host(ref), f"T={T} vs reference k_attention_flash")
+
+
+def test_reference_signature_entry_point(cuda, lib, oracle, ref_gpu):
+    """gpt2_attention_b200 has GPT2Backend.attention's exact signature (cuda/kernels.cuh:73)."""
+    T = 155
+    x = O.seeded_qkv(155, T)
+    qkv = dev16(cuda, x)
+    att = cuda.empty((T, O.E), dtype=cuda.float16, device="cuda")
+    lib.gpt2_attention_b200(att.data_ptr(), qkv.data_ptr(), T, O.E, O.H, O.D)
+    assert lib.gpt2_b200_last_error() == 0
+    cuda.cuda.synchronize()
+    assert_close(host(att), oracle.prefill(x), "void entry point")
+    naive = cuda.empty_like(att)
+    ref_gpu.attention_naive(naive.data_ptr(), qkv.data_ptr(), T)
+    assert_close(host(att), host(naive), "vs reference k_attention (naive)")
+
+
+def test_config1_golden_vector(cuda, lib):
+    """Config 1 (B=1, P=128): GPU output against the reference-generated golden att."""
+    g = np.load(os.path.join(GOLD, "prefill_T128_cfg1.npz"))
+    x = O.seeded_qkv(int(g["seed"]), int(g["T"]))
+    att = cuda.empty((128, O.E), dtype=cuda.float16, device="cuda")
+    lib.prefill(att, dev16(cuda, x), 128)
+    cuda.cuda.synchronize()
+    assert_close(host(att), g["att"], "config 1 golden")
+
+
+def test_golden_T40(cuda, lib):
+    g = np.load(os.path.join(GOLD, "prefill_T40.npz"))
+    qkv = cuda.from_numpy(g["qkv_f16"].view(np.float16).copy()).cuda()
+    att = cuda.empty((40, O.E), dtype=cuda.float16, device="cuda")
+    lib.prefill(att, qkv, 40)
+    cuda.cuda.synchronize()
+    assert_close(host(att), g["att"], "T40 golden")
+
+
+def test_batched_twelve_layers_P1024(cuda, lib, oracle):
+    """Config 2's shape: 12 independent layers of P=1024 in one launch."""
+    B, T = 12, 1024
+    xs = [O.seeded_qkv(3000 + b, T) for b in range(B)]
+    qkv = dev16(cuda, np.stack(xs))
+    att = cuda.empty((B, T, O.E), dtype=cuda.float16, device="cuda")
+    lib.prefill(att, qkv, T, B=B)
+    cuda.cuda.synchronize()
+    assert lib.status() == 0
+    got = host(att)
+    for b in (0, 5, 11):
+        assert_close(got[b], oracle.prefill(xs[b]), f"layer {b}")
+
+
+def test_batched_strides_and_canaries(cuda, lib, oracle):
+    """Padded per-sequence strides: the kernel reads only its rows and writes only its rows."""
+    B, T, pad = 3, 200, 2
+    xs = [O.seeded_qkv(4000 + b, T) for b in range(B)]
+    qkv_full = np.zeros((B, T + 1, O.QKV), np.float32)
+    qkv_full[:, :T] = np.stack(xs)
+    qkv_full[:, T] = 60000.0  # poison row after each sequence: must never be read
+    qkv = dev16(cuda, qkv_full)
+    att = cuda.full((B, T + pad, O.E), SENTINEL, dtype=cuda.float16, device="cuda")
+    lib.prefill(att, qkv, T, B=B, qkv_stride=(T + 1) * O.QKV, att_stride=(T + pad) * O.E)
+    cuda.cuda.synchronize()
+    got = host(att)
+    assert (got[:, T:] == SENTINEL).all(), "write outside [0, T)"
+    for b in range(B):
+        assert_close(got[b, :T], oracle.prefill(xs[b]), f"seq {b}")
+
+
+def test_deterministic(cuda, lib):
+    T = 700
+    qkv = dev16(cuda, O.seeded_qkv(9, T))
+    a = cuda.empty((T, O.E), dtype=cuda.float16, device="cuda")
+    b = cuda.empty_like(a)
+    lib.prefill(a, qkv, T)
+    lib.prefill(b, qkv, T)
+    cuda.cuda.synchronize()
+    assert cuda.equal(a, b)
+
+
+def test_large_scores_stay_finite(cuda, lib, oracle):
+    """Large |q.k| (values ~ N(0, 8^2)) exercises the running-max rescale path."""
+    T = 384
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((T, O.QKV)) * 8).astype(np.float16).astype(np.float32)
+    x[:, 2 * O.E:] /= 8  # keep v ~ N(0,1) so the abs tolerance stays meaningful
+    att = cuda.empty((T, O.E), dtype=cuda.float16, device="cuda")
+    lib.prefill(att, dev16(cuda, x), T)
+    cuda.cuda.synchronize()
+    assert_close(host(att), oracle.prefill(x), "large scores")
