@@ -217,9 +217,13 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
             for (int i = 0; i < BN; ++i)
                 if (i > r) x[i] = -INFINITY;
         }
-        float mx = x[0];
+        float pm[8];  // 8 independent partial maxima (no 127-long dependency chain)
 #pragma unroll
-        for (int i = 1; i < BN; ++i) mx = fmaxf(mx, x[i]);
+        for (int k = 0; k < 8; ++k) pm[k] = x[k];
+#pragma unroll
+        for (int i = 8; i < BN; ++i) pm[i & 7] = fmaxf(pm[i & 7], x[i]);
+        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
         const float mt = mx * c;
         float alpha = 1.f;
         bool resc = false;
@@ -231,15 +235,20 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
         }
         const float neg_m = -m_used;
         uint32_t pk[BN / 2];
-        float rs = 0.f;
+        // The row sum adds the fp16-ROUNDED p values (the ones the PV MMA consumes), so numerator
+        // and denominator see the same weights; 8 independent partial sums keep the adds parallel.
+        float ps[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ps[k] = 0.f;
 #pragma unroll
         for (int i = 0; i < BN / 2; ++i) {
             const float p0 = ex2_approx(fmaf(x[2 * i], c, neg_m));
             const float p1 = ex2_approx(fmaf(x[2 * i + 1], c, neg_m));
-            rs += p0 + p1;
             pk[i] = pack_half2(p0, p1);
+            ps[(2 * i) & 7] = add_f16lo_f32(pk[i], ps[(2 * i) & 7]);
+            ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[i], ps[(2 * i + 1) & 7]);
         }
-        l += rs;
+        l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
 
         if (j > 0) {  // PV_{j-1} must be done: it reads the P buffer and writes O
             ok = warp_wait(&bars->o_done, (j - 1) & 1, to);

@@ -193,6 +193,22 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// acc + (float)half_k(packed) with the sm_100 mixed-precision add (one instruction, no convert).
+__device__ __forceinline__ float add_f16lo_f32(uint32_t packed, float acc) {
+    float r;
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.f32.f16 %0, lo, %2;\n\t}"
+        : "=f"(r)
+        : "r"(packed), "f"(acc));
+    return r;
+}
+__device__ __forceinline__ float add_f16hi_f32(uint32_t packed, float acc) {
+    float r;
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.f32.f16 %0, hi, %2;\n\t}"
+        : "=f"(r)
+        : "r"(packed), "f"(acc));
+    return r;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
