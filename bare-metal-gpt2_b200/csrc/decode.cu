@@ -18,6 +18,8 @@
 //     (an atomic counter) merges all partials and writes fp16, then re-arms the counter to zero.
 // One launch therefore covers every layer / sequence of a decode step.
 #include <cmath>
+#include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -313,3 +315,128 @@ int launch_decode(__half *out, long long out_stride, const __half *q, long long 
 }
 
 }  // namespace b200
+
+// =====================================================================================
+// Decode without any allocation by the library.
+//
+// Some callers cannot let a library call cudaMalloc: a serving loop that has handed all of HBM to
+// its own pool allocator (a surprise cudaMalloc there fails or fragments the pool), a host that
+// forbids device allocations once it has finished initialising so that memory use stays fixed and
+// predictable, or a latency-critical path where cudaMalloc/cudaFree would synchronise the device.
+// gpt2_attn_decode_b200_layers grows a per-device workspace on demand; the entry point below runs
+// the same split-context kernel with its scratch (split partials, arrival counters, status word)
+// in one fixed array that is part of the library image instead.
+//
+// Limits: at most NOALLOC_PARTIALS (layer, head, split) partial records and NOALLOC_COUNTERS
+// (layer, head) pairs per call; splits are 128 keys. For GPT-2 (12 heads) that covers all 12
+// layers up to 1024 keys. Larger requests are refused before anything is launched.
+// =====================================================================================
+namespace b200 {
+namespace noalloc {
+
+constexpr int CHUNK = decode::KEYS_PER_PASS * decode::MAX_PASSES;  // 128 keys per split
+constexpr size_t NOALLOC_COUNTERS = 2048;                            // (layer, head) pairs
+constexpr size_t NOALLOC_STATUS_WORDS = 64;                          // status word + padding
+constexpr size_t NOALLOC_PARTIAL_FLOATS = 131072;                    // 512 KiB of partials
+constexpr size_t NOALLOC_PARTIALS = NOALLOC_PARTIAL_FLOATS / decode::PART_STRIDE;
+constexpr size_t NOALLOC_WORDS = NOALLOC_COUNTERS + NOALLOC_STATUS_WORDS + NOALLOC_PARTIAL_FLOATS;
+
+// The scratch itself: [counters | status | partials], 4-byte words, about 520 KiB. Every GPU that
+// loads this library holds one copy until the process exits. Device code could name it directly;
+// host code only ever uses the device address looked up below.
+static __device__ __align__(256) unsigned g_scratch[NOALLOC_WORDS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+unsigned *g_addr[kMaxDevices] = {};
+
+// Looks up the device address of g_scratch for the current device, once per device. (In host code
+// the name g_scratch is only a host-side stand-in; passing it to a kernel would be wrong.)
+unsigned *scratch_address(int *rc) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *rc = GPT2_B200_ECUDA;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_addr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+        if (e != cudaSuccess || !p) {
+            *rc = GPT2_B200_ECUDA;
+            return nullptr;
+        }
+        g_addr[dev] = static_cast<unsigned *>(p);
+    }
+    *rc = GPT2_B200_OK;
+    return g_addr[dev];
+}
+
+}  // namespace noalloc
+}  // namespace b200
+
+// Same computation and output as gpt2_attn_decode_b200_layers with a host length, but it allocates
+// nothing: the scratch is the fixed array above. The first call on each device looks up that
+// array's device address (make that first call before any stream capture). Every call on a device
+// shares the one array and leaves its contents behind; the arrival counters are cleared at the
+// start of each call, so calls must not overlap on the GPU (issue them on one stream, or order
+// them), or they race on the shared scratch.
+extern "C" int gpt2_attn_decode_b200_layers_noalloc(gpt2_half *att, long long att_layer_stride,
+                                                    const gpt2_half *q, long long q_layer_stride,
+                                                    const GPT2KVCache *kv, int L0, int nL, int len,
+                                                    cudaStream_t stream) {
+    using namespace b200;
+    const auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+    if (!kv || !kv->data || !a16(kv->data) || kv->headDim != 64 || kv->nHead < 1 || kv->nLayer < 1 ||
+        kv->maxT < 1)
+        return GPT2_B200_EINVAL;
+    if (nL < 1 || L0 < 0 || L0 + nL > kv->nLayer || !att || !q || !a16(att) || !a16(q))
+        return GPT2_B200_EINVAL;
+    if (nL > 1 && ((att_layer_stride & 7) || (q_layer_stride & 7))) return GPT2_B200_EINVAL;
+    if (len < 1 || len > kv->maxT) return GPT2_B200_EINVAL;
+    const int nsplit = (len + noalloc::CHUNK - 1) / noalloc::CHUNK;
+    const size_t pairs = static_cast<size_t>(nL) * kv->nHead;
+    if (pairs > noalloc::NOALLOC_COUNTERS || pairs * nsplit > noalloc::NOALLOC_PARTIALS) {
+        fprintf(stderr,
+                "[gpt2_b200] no-alloc decode: %zu (layer, head) pairs x %d splits exceeds the fixed "
+                "scratch (%zu pairs, %zu partials); use gpt2_attn_decode_b200_layers\n",
+                pairs, nsplit, noalloc::NOALLOC_COUNTERS, noalloc::NOALLOC_PARTIALS);
+        return GPT2_B200_EINVAL;
+    }
+    int rc = GPT2_B200_OK;
+    unsigned *base = noalloc::scratch_address(&rc);
+    if (!base) return rc;
+    unsigned *counters = base;
+    unsigned *status = base + noalloc::NOALLOC_COUNTERS;
+    float *part = reinterpret_cast<float *>(status + noalloc::NOALLOC_STATUS_WORDS);
+    if (nsplit > 1 && cudaMemsetAsync(counters, 0, pairs * sizeof(unsigned), stream) != cudaSuccess)
+        return GPT2_B200_ECUDA;
+
+    const long long slab = static_cast<long long>(kv->nHead) * kv->maxT * kv->headDim;
+    decode::Params p;
+    p.q = q;
+    p.q_stride = q_layer_stride;
+    p.kbase = kv->data + 2LL * L0 * slab;
+    p.vbase = p.kbase + slab;
+    p.kv_stride = 2 * slab;
+    p.k_ptrs = nullptr;
+    p.v_ptrs = nullptr;
+    p.out = att;
+    p.out_stride = att_layer_stride;
+    p.d_len = nullptr;
+    p.len_per_job = 0;
+    p.len_add = 0;
+    p.len = len;
+    p.H = kv->nHead;
+    p.maxT = kv->maxT;
+    p.njobs = nL;
+    p.chunk = noalloc::CHUNK;
+    p.nsplit_max = nsplit;
+    p.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
+    p.part = part;
+    p.counters = counters;
+    p.status = status;
+    dim3 grid(nsplit, kv->nHead, nL);
+    decode::k_decode_split<<<grid, decode::NT, 0, stream>>>(p);
+    return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
+}

@@ -64,6 +64,7 @@ _SIGS = {
     "gpt2_attn_decode_b200_layers": (_ci, [_vp, _cll, _vp, _cll, _kvp, _ci, _ci, _vp, _ci, _ci, _vp]),
     "gpt2_attn_decode_b200_batched": (_ci, [_vp, _cll, _vp, _cll, _vp, _vp, _vp, _ci, _ci, _ci, _ci,
                                             _vp]),
+    "gpt2_attn_decode_b200_layers_noalloc": (_ci, [_vp, _cll, _vp, _cll, _kvp, _ci, _ci, _ci, _vp]),
     "gpt2_b200_decode_attn_step": (_ci, [_vp, _cll, _vp, _cll, _kvp, _vp, _ci, _vp]),
     "gpt2_kv_alloc_b200": (_ci, [_kvp, _ci]),
     "gpt2_kv_alloc_shape_b200": (_ci, [_kvp, _ci, _ci, _ci, _ci]),

@@ -113,6 +113,20 @@ int gpt2_attn_decode_b200_layers(gpt2_half *att, long long att_layer_stride, con
                                  long long q_layer_stride, const GPT2KVCache *kv, int L0, int nL,
                                  const int *d_len, int len, int max_len, cudaStream_t stream);
 
+/* gpt2_attn_decode_b200_layers with a host length, for callers that must not have the library
+ * allocate device memory (a pool allocator that owns all of HBM, a host that freezes allocations
+ * after start-up, a latency-critical loop that cannot absorb a synchronising cudaMalloc). No
+ * counterpart in the reference. It allocates nothing: its scratch is a fixed ~520 KiB array inside
+ * the library image, one per GPU, held until the process exits. Limits: nL * nHead <= 2048 and
+ * nL * nHead * ceil(len / 128) <= 1985 (all 12 GPT-2 layers up to 1024 keys); larger requests
+ * return GPT2_B200_EINVAL before launching. The first call on a device looks up the array's device
+ * address, so make it before any stream capture. All calls on a device share the array (its counters
+ * are cleared at the start of each call): calls that overlap on the GPU race, so keep them ordered. */
+int gpt2_attn_decode_b200_layers_noalloc(gpt2_half *att, long long att_layer_stride,
+                                         const gpt2_half *q, long long q_layer_stride,
+                                         const GPT2KVCache *kv, int L0, int nL, int len,
+                                         cudaStream_t stream);
+
 /* Decode attention for B independent sequences, one layer each, in ONE launch: sequence b attends
  * over the [H][maxT][D] K and V slabs at k_slabs[b] / v_slabs[b] (device arrays of device pointers)
  * for d_lens[b] keys (device ints), query q + b*q_stride, output att + b*att_stride. max_len bounds
