@@ -18,6 +18,7 @@ enum StatusBits : unsigned {
     ST_PREFILL_SMEM_ALIGN = 1u << 3,       // dynamic shared memory not 1024-byte aligned
     ST_PREFILL_DRAIN_TIMEOUT = 1u << 4,    // teardown could not confirm in-flight copies / MMAs
     ST_DECODE_BAD_LEN = 1u << 8,           // device-side length outside [1, maxT]
+    ST_DECODE_TIMEOUT = 1u << 10,          // a decode stage wait gave up
     ST_KV_BAD_POS = 1u << 9,               // device-side append position outside [0, maxT)
     ST_TEST_WAIT_TIMEOUT = 1u << 16,       // the wait-timeout self-test expired (expected)
 };
@@ -33,6 +34,7 @@ struct DeviceContext {
     size_t part_floats = 0;
     size_t counter_words = 0;
     bool prefill_attr_done = false;
+    bool decode_attr_done = false;
     int num_sms = 0;
 };
 

@@ -226,18 +226,6 @@ __global__ void __launch_bounds__(NT) k_decode_split(const Params p) {
 
 }  // namespace decode
 
-// Chooses the split size: enough CTAs to cover the SMs a few times, chunks of 16..128 keys.
-static int choose_chunk(int max_len, long long pairs, int num_sms) {
-    const long long target_ctas = 4LL * (num_sms > 0 ? num_sms : 148);
-    long long nsplit = (target_ctas + pairs - 1) / pairs;
-    if (nsplit < 1) nsplit = 1;
-    long long chunk = (max_len + nsplit - 1) / nsplit;
-    chunk = ((chunk + 15) / 16) * 16;
-    if (chunk < 16) chunk = 16;
-    if (chunk > decode::KEYS_PER_PASS * decode::MAX_PASSES) chunk = decode::KEYS_PER_PASS * decode::MAX_PASSES;
-    return static_cast<int>(chunk);
-}
-
 // Ensures the workspace holds `floats` partial floats and `words` counters (zeroed). Refuses to
 // allocate while `stream` is being captured.
 int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream) {
@@ -264,54 +252,31 @@ int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cud
     return GPT2_B200_OK;
 }
 
+int decode_stream_splits(int max_len, long long pairs, int num_sms);
+int launch_decode_stream(__half *out, long long out_stride, const __half *q, long long q_stride,
+                         const __half *kbase, const __half *vbase, long long kv_stride,
+                         const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
+                         int len_per_job, int len_add, int len, int max_len, int njobs, int H,
+                         int maxT, cudaStream_t stream);
+
+// Workspace the decode launches need for `jobs` (layer x sequence) decodes of up to max_len keys.
 size_t decode_workspace_floats(int jobs, int H, int max_len, int num_sms, size_t *words) {
-    const int chunk = choose_chunk(max_len, static_cast<long long>(jobs) * H, num_sms);
-    const int nsplit = (max_len + chunk - 1) / chunk;
+    const int nsplit = decode_stream_splits(max_len, static_cast<long long>(jobs) * H, num_sms);
     if (words) *words = static_cast<size_t>(jobs) * H;
-    return static_cast<size_t>(jobs) * H * nsplit * decode::PART_STRIDE;
+    return nsplit > 1 ? static_cast<size_t>(jobs) * H * nsplit * (decode::HD + 2) : 0;
 }
 
-// Launches split-context decode for `njobs` jobs. Exactly one of (kbase, vbase, kv_stride) or
-// (k_ptrs, v_ptrs) describes the slabs. Arguments are validated by the caller.
+// Decode for `njobs` jobs: the streamed kernel (decode_stream.cu). Exactly one of
+// (kbase, vbase, kv_stride) or (k_ptrs, v_ptrs) describes the slabs. Arguments are validated by the
+// caller.
 int launch_decode(__half *out, long long out_stride, const __half *q, long long q_stride,
                   const __half *kbase, const __half *vbase, long long kv_stride,
                   const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
                   int len_per_job, int len_add, int len, int max_len, int njobs, int H, int maxT,
                   cudaStream_t stream) {
-    DeviceContext *ctx = device_context();
-    if (!ctx) return GPT2_B200_ECUDA;
-    decode::Params p;
-    p.q = q;
-    p.q_stride = q_stride;
-    p.kbase = kbase;
-    p.vbase = vbase;
-    p.kv_stride = kv_stride;
-    p.k_ptrs = k_ptrs;
-    p.v_ptrs = v_ptrs;
-    p.out = out;
-    p.out_stride = out_stride;
-    p.d_len = d_len;
-    p.len_per_job = len_per_job;
-    p.len_add = len_add;
-    p.len = len;
-    p.H = H;
-    p.maxT = maxT;
-    p.njobs = njobs;
-    p.chunk = choose_chunk(max_len, static_cast<long long>(njobs) * H, ctx->num_sms);
-    p.nsplit_max = (max_len + p.chunk - 1) / p.chunk;
-    p.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
-    p.status = ctx->status;
-    if (p.nsplit_max > 1) {
-        const size_t floats = static_cast<size_t>(njobs) * H * p.nsplit_max * decode::PART_STRIDE;
-        const size_t words = static_cast<size_t>(njobs) * H;
-        const int rc = ensure_decode_workspace(ctx, floats, words, stream);
-        if (rc != GPT2_B200_OK) return rc;
-    }
-    p.part = ctx->part;
-    p.counters = ctx->counters;
-    dim3 grid(p.nsplit_max, H, njobs);
-    decode::k_decode_split<<<grid, decode::NT, 0, stream>>>(p);
-    return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
+    return launch_decode_stream(out, out_stride, q, q_stride, kbase, vbase, kv_stride, k_ptrs,
+                                v_ptrs, d_len, len_per_job, len_add, len, max_len, njobs, H, maxT,
+                                stream);
 }
 
 }  // namespace b200

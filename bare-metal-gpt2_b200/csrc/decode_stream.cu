@@ -1,0 +1,368 @@
+// decode_stream.cu — M=1 decode attention over the KV cache, streamed through shared memory.
+//
+// Same operation as the reference's k_attn_decode (cuda/kvcache.cu:88-129): for one query per
+// (job, head) — a job is a layer of one cache or one sequence — att[h*64:(h+1)*64] =
+// sum_{j<len} softmax_j(q.k_j / 8) v_j over the head-major [H][maxT][64] fp16 K and V slabs.
+//
+// Decode is a pure HBM stream (36,864 bytes of K+V per key for the 12-layer step), so the kernel is
+// built to keep every SM's share of HBM busy from start to finish:
+//   - grid = (split, head, job) sized to about one CTA per SM; for the 12-layer GPT-2 step that is
+//     one CTA per (layer, head) streaming its whole context, so no cross-CTA merge is needed at all;
+//   - warp 8 (one thread) issues cp.async.bulk copies of 64-key stages (8 KB of K + 8 KB of V, the
+//     slabs are contiguous) into a 4-stage shared-memory ring, tracked by mbarriers;
+//   - warps 0-7 each own 8 keys of every stage: 4 lanes per key (16 dims each, q held pre-scaled by
+//     log2(e)/8 in registers), two xor-shuffles per score, a warp-level online softmax (running max,
+//     sum and 2 output dims per lane) with the hardware ex2, and V rows read as 128-byte lines;
+//   - the 8 warps' (m, l, o) are merged once in shared memory; only when a (job, head) is split over
+//     several CTAs (few jobs, e.g. one layer) do partials go through the workspace and the last CTA to
+//     arrive merges them (atomic counter, re-armed to zero for the next call / graph replay).
+// Every mbarrier wait is bounded; a timeout sets a status bit and the CTA unwinds after its own
+// copies have landed.
+#include <cmath>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace b200 {
+namespace dstream {
+
+constexpr int HD = 64;
+constexpr int NCW = 8;                       // consumer warps
+constexpr int NT = 32 * (NCW + 1);           // + one producer warp
+constexpr int KPS = 64;                      // keys per stage
+constexpr int NSTAGE = 4;
+constexpr int ROW_BYTES = HD * 2;            // 128 B per key row
+constexpr int STAGE_BYTES = KPS * ROW_BYTES; // 8 KB of K (and 8 KB of V)
+constexpr int OFF_K = 0;
+constexpr int OFF_V = OFF_K + NSTAGE * STAGE_BYTES;
+constexpr int OFF_RED = OFF_V + NSTAGE * STAGE_BYTES;           // [NCW][64] o + [NCW] m + [NCW] l
+constexpr int OFF_BAR = OFF_RED + (NCW * HD + 2 * NCW) * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 128;
+constexpr int PART_STRIDE = HD + 2;
+
+struct __align__(8) Bars {
+    uint64_t full[NSTAGE];
+    uint64_t empty[NSTAGE];
+    int abort;
+    int is_last;
+};
+
+struct Params {
+    const __half *q;
+    long long q_stride;
+    const __half *kbase;
+    const __half *vbase;
+    long long kv_stride;
+    const __half *const *k_ptrs;
+    const __half *const *v_ptrs;
+    __half *out;
+    long long out_stride;
+    const int *d_len;
+    int len_per_job;
+    int len_add;
+    int len;
+    int H, maxT, njobs;
+    int nsplit;               // grid.x: CTAs per (job, head) at most
+    float scale_log2;
+    float *part;              // [njobs][H][nsplit][PART_STRIDE] (used only when a pair is split)
+    unsigned *counters;       // [njobs][H]
+    unsigned *status;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned long long to) {
+    const bool ok = mbar_wait(bar, parity, to);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(NT) k_decode_stream(const Params p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
+    float *red_o = reinterpret_cast<float *>(smem + OFF_RED);
+    float *red_m = red_o + NCW * HD;
+    float *red_l = red_m + NCW;
+    const int split = blockIdx.x, h = blockIdx.y, job = blockIdx.z;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const unsigned long long to = p.timeout_ns;
+
+    int len = p.len;
+    if (p.d_len) len = (p.len_per_job ? p.d_len[job] : p.d_len[0]) + p.len_add;
+    if (len < 1 || len > p.maxT) {
+        if (t == 0 && split == 0) atomicOr(p.status, ST_DECODE_BAD_LEN);
+        return;
+    }
+    // Split of [0, len): chunks of whole stages; CTAs past the last chunk have nothing to do.
+    const int per = (len + p.nsplit - 1) / p.nsplit;
+    const int chunk = ((per + KPS - 1) / KPS) * KPS;
+    const int nsplit = (len + chunk - 1) / chunk;
+    if (split >= nsplit) return;
+    const int k0 = split * chunk;
+    const int k1 = min(k0 + chunk, len);
+    const int nstages = (k1 - k0 + KPS - 1) / KPS;
+
+    const __half *K = p.k_ptrs ? p.k_ptrs[job] : p.kbase + job * p.kv_stride;
+    const __half *V = p.v_ptrs ? p.v_ptrs[job] : p.vbase + job * p.kv_stride;
+    K += static_cast<long long>(h) * p.maxT * HD;
+    V += static_cast<long long>(h) * p.maxT * HD;
+
+    if (t == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], NCW);
+        }
+        bars->abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ------------------------------------------------------------ producer (one thread)
+        if (lane == 0) {
+            bool ok = true;
+            int issued = 0;
+            for (int i = 0; i < nstages; ++i) {
+                const int s = i % NSTAGE;
+                if (i >= NSTAGE) {
+                    ok = mbar_wait(&bars->empty[s], ((i / NSTAGE) - 1) & 1, to);
+                    if (!ok) break;
+                }
+                if (*reinterpret_cast<volatile int *>(&bars->abort)) break;
+                const int key = k0 + i * KPS;
+                const uint32_t bytes = static_cast<uint32_t>(min(KPS, k1 - key)) * ROW_BYTES;
+                mbar_arrive_expect_tx(&bars->full[s], 2 * bytes);
+                bulk_load(smem + OFF_K + s * STAGE_BYTES, K + static_cast<long long>(key) * HD, bytes,
+                          &bars->full[s]);
+                bulk_load(smem + OFF_V + s * STAGE_BYTES, V + static_cast<long long>(key) * HD, bytes,
+                          &bars->full[s]);
+                issued = i + 1;
+            }
+            if (!ok) {
+                atomicOr(p.status, ST_DECODE_TIMEOUT);
+                *reinterpret_cast<volatile int *>(&bars->abort) = 1;
+            }
+            // every issued copy lands before the CTA may exit
+            bool drained = true;
+            for (int i = (issued > NSTAGE ? issued - NSTAGE : 0); i < issued; ++i)
+                drained = mbar_wait(&bars->full[i % NSTAGE], (i / NSTAGE) & 1, to) && drained;
+            if (!drained) atomicOr(p.status, ST_DECODE_TIMEOUT);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ consumers (8 warps)
+        const int kq = lane >> 2;        // key of this warp's 8 handled by this lane group
+        const int dq = (lane & 3) * 16;  // 16 dims of that key handled by this lane
+        float qv[16];
+        {
+            const uint4 *q4 = reinterpret_cast<const uint4 *>(p.q + job * p.q_stride + h * HD + dq);
+            const uint4 a = q4[0], b = q4[1];
+            const __half2 *h2a = reinterpret_cast<const __half2 *>(&a);
+            const __half2 *h2b = reinterpret_cast<const __half2 *>(&b);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 fa = __half22float2(h2a[i]);
+                const float2 fb = __half22float2(h2b[i]);
+                qv[2 * i] = fa.x * p.scale_log2;
+                qv[2 * i + 1] = fa.y * p.scale_log2;
+                qv[8 + 2 * i] = fb.x * p.scale_log2;
+                qv[8 + 2 * i + 1] = fb.y * p.scale_log2;
+            }
+        }
+        float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;  // o: dims 2*lane, 2*lane+1
+        bool ok = true;
+        for (int i = 0; i < nstages; ++i) {
+            const int s = i % NSTAGE;
+            ok = warp_wait(&bars->full[s], (i / NSTAGE) & 1, to);
+            if (!ok) break;
+            const int rows = min(KPS, k1 - (k0 + i * KPS));
+            const int krow = warp * 8 + kq;  // row of the stage this lane scores
+            const bool valid = krow < rows;
+            const uint8_t *kr = smem + OFF_K + s * STAGE_BYTES + krow * ROW_BYTES + dq * 2;
+            float sc = -INFINITY;
+            {
+                const uint4 a = reinterpret_cast<const uint4 *>(kr)[0];
+                const uint4 b = reinterpret_cast<const uint4 *>(kr)[1];
+                const __half2 *h2a = reinterpret_cast<const __half2 *>(&a);
+                const __half2 *h2b = reinterpret_cast<const __half2 *>(&b);
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 fa = __half22float2(h2a[e]);
+                    const float2 fb = __half22float2(h2b[e]);
+                    d = fmaf(qv[2 * e], fa.x, d);
+                    d = fmaf(qv[2 * e + 1], fa.y, d);
+                    d = fmaf(qv[8 + 2 * e], fb.x, d);
+                    d = fmaf(qv[8 + 2 * e + 1], fb.y, d);
+                }
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                if (valid) sc = d;
+            }
+            float mt = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+            if (mt > m) {  // warp-uniform; m_t is finite whenever this warp has a valid key
+                const float alpha = ex2_approx(m - mt);  // 0 on the first stage with keys
+                l *= alpha;
+                o0 *= alpha;
+                o1 *= alpha;
+                m = mt;
+            }
+            const float pk = valid ? ex2_approx(sc - m) : 0.f;
+            float ps = pk;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l += ps;
+            const uint8_t *vbase = smem + OFF_V + s * STAGE_BYTES + warp * 8 * ROW_BYTES + lane * 4;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float pkk = __shfl_sync(0xffffffffu, pk, 4 * k);
+                if (warp * 8 + k < rows) {  // warp-uniform; never touch rows the copy did not fill
+                    const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(vbase + k * ROW_BYTES));
+                    o0 = fmaf(pkk, v.x, o0);
+                    o1 = fmaf(pkk, v.y, o1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->empty[s]);
+        }
+        if (!ok) {
+            atomicOr(p.status, ST_DECODE_TIMEOUT);
+            *reinterpret_cast<volatile int *>(&bars->abort) = 1;
+            m = -INFINITY;
+        }
+        red_o[warp * HD + 2 * lane] = o0;
+        red_o[warp * HD + 2 * lane + 1] = o1;
+        if (lane == 0) {
+            red_m[warp] = m;
+            red_l[warp] = l;
+        }
+    }
+    __syncthreads();
+    if (*reinterpret_cast<volatile int *>(&bars->abort)) return;
+
+    // ---------------------------------------------------------------- merge the 8 warps
+    const int jh = job * p.H + h;
+    float M = red_m[0];
+#pragma unroll
+    for (int w = 1; w < NCW; ++w) M = fmaxf(M, red_m[w]);
+    if (nsplit == 1) {
+        if (t < HD / 2) {
+            float L = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int w = 0; w < NCW; ++w) {
+                const float wt = red_m[w] == -INFINITY ? 0.f : ex2_approx(red_m[w] - M);
+                L = fmaf(wt, red_l[w], L);
+                a0 = fmaf(wt, red_o[w * HD + 2 * t], a0);
+                a1 = fmaf(wt, red_o[w * HD + 2 * t + 1], a1);
+            }
+            const float inv = 1.f / L;
+            reinterpret_cast<__half2 *>(p.out + job * p.out_stride + h * HD)[t] =
+                __floats2half2_rn(a0 * inv, a1 * inv);
+        }
+        return;
+    }
+    float *mine = p.part + (static_cast<long long>(jh) * p.nsplit + split) * PART_STRIDE;
+    if (t < HD) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w)
+            a = fmaf(red_m[w] == -INFINITY ? 0.f : ex2_approx(red_m[w] - M), red_o[w * HD + t], a);
+        mine[t] = a;
+    }
+    if (t == HD) mine[HD] = M;
+    if (t == HD + 1) {
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) L = fmaf(red_m[w] == -INFINITY ? 0.f : ex2_approx(red_m[w] - M), red_l[w], L);
+        mine[HD + 1] = L;
+    }
+    __threadfence();
+    __syncthreads();
+    if (t == 0) {
+        const unsigned prev = atomicAdd(&p.counters[jh], 1u);
+        bars->is_last = (prev == static_cast<unsigned>(nsplit - 1));
+    }
+    __syncthreads();
+    if (!bars->is_last) return;
+    __threadfence();
+    const float *base = p.part + static_cast<long long>(jh) * p.nsplit * PART_STRIDE;
+    if (t < HD) {
+        float MM = -INFINITY;
+        for (int sidx = 0; sidx < nsplit; ++sidx) MM = fmaxf(MM, __ldcg(base + sidx * PART_STRIDE + HD));
+        float L = 0.f, O = 0.f;
+        for (int sidx = 0; sidx < nsplit; ++sidx) {
+            const float *ps = base + sidx * PART_STRIDE;
+            const float w = ex2_approx(__ldcg(ps + HD) - MM);
+            L = fmaf(w, __ldcg(ps + HD + 1), L);
+            O = fmaf(w, __ldcg(ps + t), O);
+        }
+        p.out[job * p.out_stride + h * HD + t] = __float2half_rn(O / L);
+    }
+    if (t == 0) p.counters[jh] = 0u;
+}
+
+}  // namespace dstream
+
+int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream);
+
+// CTAs per (job, head): about one CTA per SM in total, at least one stage per CTA.
+int decode_stream_splits(int max_len, long long pairs, int num_sms) {
+    const int sms = num_sms > 0 ? num_sms : 148;
+    long long n = (sms + pairs / 2) / pairs;  // round(sms / pairs)
+    if (n < 1) n = 1;
+    const long long max_n = (max_len + dstream::KPS - 1) / dstream::KPS;
+    if (n > max_n) n = max_n;
+    return static_cast<int>(n);
+}
+
+int launch_decode_stream(__half *out, long long out_stride, const __half *q, long long q_stride,
+                         const __half *kbase, const __half *vbase, long long kv_stride,
+                         const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
+                         int len_per_job, int len_add, int len, int max_len, int njobs, int H,
+                         int maxT, cudaStream_t stream) {
+    DeviceContext *ctx = device_context();
+    if (!ctx) return GPT2_B200_ECUDA;
+    if (!ctx->decode_attr_done) {
+        if (cudaFuncSetAttribute(dstream::k_decode_stream, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 dstream::SMEM_BYTES) != cudaSuccess)
+            return GPT2_B200_ECUDA;
+        ctx->decode_attr_done = true;
+    }
+    dstream::Params p;
+    p.q = q;
+    p.q_stride = q_stride;
+    p.kbase = kbase;
+    p.vbase = vbase;
+    p.kv_stride = kv_stride;
+    p.k_ptrs = k_ptrs;
+    p.v_ptrs = v_ptrs;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.d_len = d_len;
+    p.len_per_job = len_per_job;
+    p.len_add = len_add;
+    p.len = len;
+    p.H = H;
+    p.maxT = maxT;
+    p.njobs = njobs;
+    p.nsplit = decode_stream_splits(max_len, static_cast<long long>(njobs) * H, ctx->num_sms);
+    p.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
+    p.status = ctx->status;
+    p.timeout_ns = wait_timeout_ns();
+    p.part = nullptr;
+    p.counters = nullptr;
+    if (p.nsplit > 1) {
+        const size_t floats = static_cast<size_t>(njobs) * H * p.nsplit * dstream::PART_STRIDE;
+        const size_t words = static_cast<size_t>(njobs) * H;
+        const int rc = ensure_decode_workspace(ctx, floats, words, stream);
+        if (rc != GPT2_B200_OK) return rc;
+        p.part = ctx->part;
+        p.counters = ctx->counters;
+    }
+    dim3 grid(p.nsplit, H, njobs);
+    dstream::k_decode_stream<<<grid, dstream::NT, dstream::SMEM_BYTES, stream>>>(p);
+    return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
+}
+
+}  // namespace b200

@@ -3,24 +3,37 @@
 // Computes what the reference's k_attention_flash computes (cuda/kernels_fused.cu:58-140): for every
 // head h of qkv[T, 3E] (q | k | v, head h at h*64), att[i, h*64:(h+1)*64] = sum_{j<=i} softmax_j(q_i.k_j
 // / 8) v_j, fp16 in, fp32 accumulation, fp16 out. The reference runs one warp per query on CUDA cores
-// with 32-key tiles; here one CTA owns a 128-query tile of one head and streams 128-key tiles:
+// with 32-key tiles.
 //
-//   warp 0  (1 thread)  TMA producer: Q tile once, then K_j / V_j tiles (128 x 64 fp16, 128-byte
-//                       swizzle) straight out of the packed qkv rows into a 2-stage ring.
-//   warp 1  (1 thread)  MMA issuer: S = Q K_j^T into TMEM (M128 N128 K64, 4 x tcgen05.mma K16), and
-//                       O += P_j V_j into TMEM (M128 N64 K128, 8 x tcgen05.mma K16). S_{j+1} is issued
-//                       as soon as the softmax warps have read S_j, so it overlaps their exp work.
-//   warps 2-5 (128 thr) softmax: thread r owns query row r = TMEM lane r. Reads S_j (tcgen05.ld),
-//                       applies the causal mask on the diagonal tile only, keeps a running max m and
-//                       sum l in the log2 domain (scale folded into one FFMA), writes P_j = 2^(s-m) as
-//                       fp16 into shared memory in the MMA's swizzled K-major layout, and rescales O in
-//                       TMEM only when the running max grows by more than 2^8 (otherwise the stale max
-//                       is kept for both l and O, which leaves the result unchanged). Epilogue: O / l
-//                       -> fp16 -> att.
+// Here a work item is a PAIR of 128-query tiles (A = tile 2p, B = tile 2p+1) of one head of one
+// sequence, processed against 128-key tiles 0..2p+1 (A stops at its diagonal tile 2p). Each K/V tile
+// is loaded once into shared memory and used by both query tiles, which halves the K/V traffic per
+// FLOP (with one query tile per CTA the K/V re-reads alone kept L2 busy enough to stretch a tile load to
+// ~2 us). The kernel is persistent: one CTA per SM loops over its items (heavy and light pairs in a
+// snake order), with TMEM and barriers set up once and the loads / MMAs of the next item running
+// while the current one finishes. Roles:
 //
-// TMEM: 256 columns per CTA (S: 128 fp32 columns, O: 64), so two CTAs share an SM (smem 112 KB each)
-// and the tensor core alternates between them. Tiles are scheduled heaviest-first (the last query
-// tile of a sequence has the most keys). No cluster, no multicast. Every mbarrier wait is bounded.
+//   warp 0   (1 thread)  TMA producer: the two Q tiles of each item (double-buffered), then K(t) and
+//                        V(t-1) tiles (128 x 64 fp16, 128-byte swizzle) straight out of the packed qkv
+//                        rows into 4-stage K and V rings, running ahead across item boundaries.
+//   warps 1, 18 (1 thr)  MMA issuers, one per query tile x: per K/V tile, S_x = Q_x K^T (M128 N128 K64,
+//                        4 x tcgen05.mma K16, operands in shared memory), then O_x += P_x V (M128 N64
+//                        K128, 8 x tcgen05.mma K16, P read from TMEM). Two independent issue streams
+//                        and four accumulators keep the tensor pipe busy; shared-memory descriptors are
+//                        built once and advanced by 32-bit adds.
+//   warps 2-9, 10-17     softmax of query tile A, of query tile B: TMEM lane r = query row r; each
+//                        row's 128 scores are split between two warps (keys 0-63 / 64-127) that
+//                        exchange their partial maxima through shared memory and a two-arrival
+//                        mbarrier. Log2 domain (1/8 * log2(e) folded into one FFMA, hardware ex2);
+//                        causal mask on the diagonal tile only; P = 2^(s-m) written as packed fp16
+//                        straight into TMEM (one tcgen05.st per thread); the row sum adds the
+//                        fp16-rounded P values (numerator and denominator use identical weights); O is
+//                        rescaled in TMEM only when the running max grows by more than 2^8 (the stale
+//                        max is otherwise kept for both l and O: exact, and P <= 256). Epilogue:
+//                        O / l -> fp16 -> att, then O is released for the next item.
+//
+// TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 196 KB.
+// No cluster, no multicast. Every mbarrier wait is bounded.
 #include <cmath>
 #include <cstdio>
 
@@ -33,46 +46,105 @@ namespace prefill {
 constexpr int BM = 128;  // query rows per tile = TMEM lanes
 constexpr int BN = 128;  // keys per KV tile
 constexpr int HD = 64;   // head dim
-constexpr int NSTAGE = 2;
+constexpr int NSTAGE = 4;  // K ring and V ring depth
+constexpr int NQ = 2;      // Q buffers (each holds the two query tiles of an item)
 constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB: 128 rows x 128 B
-constexpr int P_BLOCK_BYTES = BM * 64 * 2;  // P is two 64-key column blocks of 16 KB
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;
+constexpr int OFF_Q = 0;                                     // [NQ][2 tiles]
+constexpr int OFF_K = OFF_Q + NQ * 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + NSTAGE * TILE_BYTES;
-constexpr int OFF_P = OFF_V + NSTAGE * TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BLOCK_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 128;
-constexpr int NTHREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t TCOL_S = 0;
-constexpr uint32_t TCOL_O = 128;
+constexpr int OFF_BAR = OFF_V + NSTAGE * TILE_BYTES;
+constexpr int SMEM_BYTES = OFF_BAR + 512;
+constexpr int NSOFT_WARPS = 4;  // per query tile: one warp per TMEM lane quarter
+constexpr int NTHREADS = 32 * (3 + 2 * NSOFT_WARPS);  // producer, 2 MMA issuers, 2 softmax groups
+constexpr int MMA_B_WARP = 2 + 2 * NSOFT_WARPS;              // warp 10 issues query tile B's MMAs
+constexpr int CTAS_PER_SM = 1;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t TCOL_S = 0;    // + 128 * stream
+constexpr uint32_t TCOL_O = 256;  // + 64 * stream
+constexpr uint32_t TCOL_P = 384;  // + 64 * stream
 constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);  // Q K-major, K K-major
-constexpr uint32_t IDESC_O = idesc_f16_f32(BM, HD, 0, 1);  // P K-major, V MN-major
+constexpr uint32_t IDESC_O = idesc_f16_f32(BM, HD, 0, 1);  // P K-major (TMEM), V MN-major
 constexpr float RESCALE_THRESHOLD = 8.0f;                  // log2 units: P stays <= 2^8
 
+struct Stream {  // per query tile of the pair
+    uint64_t s_full;   // its QK of the current K/V tile is done
+    uint64_t s_free;   // its softmax warps have read S
+    uint64_t p_full;   // its softmax warps have written P (and rescaled O)
+    uint64_t o_done;   // its PV of the current tile is done
+    uint64_t o_free;   // its epilogue has read O of the current item
+    uint64_t drain;    // teardown: every MMA of this query tile's issuing thread has completed
+    int ex2_done[4];   // per lane quarter (= SM sub-partition): ex2 phases completed by its warp
+};
+
 struct __align__(8) Bars {
-    uint64_t q_full;
+    uint64_t q_full[NQ];
+    uint64_t q_empty[NQ];
     uint64_t k_full[NSTAGE];
+    uint64_t k_empty[NSTAGE];  // the QKs that read this K stage have completed
     uint64_t v_full[NSTAGE];
-    uint64_t kv_empty[NSTAGE];
-    uint64_t s_full;
-    uint64_t s_free;
-    uint64_t p_full;
-    uint64_t o_done;
-    uint64_t drain;
+    uint64_t v_empty[NSTAGE];  // the PVs that read this V stage have completed
+    Stream st[2];
     uint32_t tmem_base;
     int abort;
 };
-static_assert(sizeof(Bars) <= 128, "barrier block");
+static_assert(sizeof(Bars) <= 512, "barrier block");
 
 struct Params {
     __half *att;
     long long att_seq_stride;  // elements between sequences of att
     int T, H, E, B;
     int n_qtiles;
+    int n_pairs;               // ceil(n_qtiles / 2)
+    int total_items;           // n_pairs * H * B
     float scale_log2;          // log2(e) / sqrt(D)
     unsigned *status;
     unsigned long long timeout_ns;
+};
+
+struct Item {
+    int pair, h, b;
+    int nk[2];  // K/V tiles of query tile A (2p+1) and of B (2p+2, or 0 when tile 2p+1 is past T)
+    int nkv;    // K/V tiles loaded for the item: max(nk)
+};
+
+// The r-th item of this CTA. Items are numbered heaviest first (the last pair of every head and
+// sequence first); rounds alternate direction (snake) so that each CTA gets a mix of heavy and light
+// pairs. Returns false when this CTA has no r-th item (nor any later one).
+__device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long i = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - c) : c);
+    if (i >= p.total_items) return false;
+    const int per = p.H * p.B;
+    const int idx = static_cast<int>(i);
+    it.pair = p.n_pairs - 1 - idx / per;
+    const int rem = idx % per;
+    it.h = rem % p.H;
+    it.b = rem / p.H;
+    it.nk[0] = 2 * it.pair + 1;
+    it.nk[1] = (2 * it.pair + 1 < p.n_qtiles) ? 2 * it.pair + 2 : 0;
+    it.nkv = it.nk[1] ? it.nk[1] : it.nk[0];
+    return true;
+}
+
+// A cursor over this CTA's K/V tiles in processing order (item by item).
+struct Cursor {
+    Item I;
+    int it, j, g;  // item number, K/V tile within the item, K/V tile number over all items
+    bool valid;
+    __device__ __forceinline__ void start(const Params &p) {
+        it = 0;
+        j = 0;
+        g = 0;
+        valid = get_item(p, 0, I);
+    }
+    __device__ __forceinline__ void advance(const Params &p) {
+        ++g;
+        if (++j == I.nkv) {
+            j = 0;
+            ++it;
+            valid = get_item(p, it, I);
+        }
+    }
 };
 
 __device__ __forceinline__ void raise_abort(Bars *bars, unsigned *status, unsigned bit) {
@@ -85,263 +157,375 @@ __device__ __forceinline__ bool aborted(Bars *bars) {
 }
 
 // ------------------------------------------------------------------ producer (one thread)
-__device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, const Params &p,
-                             int b, int h, int qt, int nk) {
+// Load order: the Q tiles of an item before its first K; then K(t), V(t-1), K(t+1), V(t), ... . K
+// stages are released when their QKs complete and V stages when their PVs complete (later), so
+// issuing V one tile behind K keeps the K loads from queueing behind a V wait.
+__device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, const Params &p) {
     const unsigned long long to = p.timeout_ns;
-    mbar_arrive_expect_tx(&bars->q_full, TILE_BYTES);
-    tma_load_3d(smem + OFF_Q, tm, &bars->q_full, h * HD, qt * BM, b);
-    int last_issue[NSTAGE] = {-1, -1};
+    int last_q[NQ] = {-1, -1}, last_k[NSTAGE], last_v[NSTAGE];
+    for (int s = 0; s < NSTAGE; ++s) last_k[s] = last_v[s] = -1;
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-        const int st = j % NSTAGE;
-        if (j >= NSTAGE) {
-            ok = mbar_wait(&bars->kv_empty[st], ((j / NSTAGE) - 1) & 1, to);
-            if (!ok) break;
+    Cursor kc, vc;  // next K tile to load; next V tile to load (never ahead of kc)
+    kc.start(p);
+    vc.start(p);
+    auto load_v = [&]() -> bool {
+        const int s = vc.g % NSTAGE;
+        if (vc.g >= NSTAGE && !mbar_wait(&bars->v_empty[s], ((vc.g / NSTAGE) - 1) & 1, to)) return false;
+        mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
+        tma_load_3d(smem + OFF_V + s * TILE_BYTES, tm, &bars->v_full[s], 2 * p.E + vc.I.h * HD,
+                    vc.j * BN, vc.I.b);
+        last_v[s] = vc.g;
+        vc.advance(p);
+        return true;
+    };
+    while (ok && kc.valid) {
+        if (aborted(bars)) {
+            ok = false;
+            break;
         }
-        if (aborted(bars)) break;
-        mbar_arrive_expect_tx(&bars->k_full[st], TILE_BYTES);
-        tma_load_3d(smem + OFF_K + st * TILE_BYTES, tm, &bars->k_full[st], p.E + h * HD, j * BN, b);
-        mbar_arrive_expect_tx(&bars->v_full[st], TILE_BYTES);
-        tma_load_3d(smem + OFF_V + st * TILE_BYTES, tm, &bars->v_full[st], 2 * p.E + h * HD,
-                    j * BN, b);
-        last_issue[st] = j;
+        if (kc.j == 0) {  // new item: its two Q tiles (the buffer's previous item issued its last QK)
+            const int qb = kc.it % NQ;
+            if (kc.it >= NQ && !(ok = mbar_wait(&bars->q_empty[qb], ((kc.it / NQ) - 1) & 1, to))) break;
+            const int ntiles = kc.I.nk[1] ? 2 : 1;
+            mbar_arrive_expect_tx(&bars->q_full[qb], ntiles * TILE_BYTES);
+            for (int t = 0; t < ntiles; ++t)
+                tma_load_3d(smem + OFF_Q + (qb * 2 + t) * TILE_BYTES, tm, &bars->q_full[qb],
+                            kc.I.h * HD, (2 * kc.I.pair + t) * BM, kc.I.b);
+            last_q[qb] = kc.it;
+        }
+        const int s = kc.g % NSTAGE;
+        if (kc.g >= NSTAGE && !(ok = mbar_wait(&bars->k_empty[s], ((kc.g / NSTAGE) - 1) & 1, to)))
+            break;
+        mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
+        tma_load_3d(smem + OFF_K + s * TILE_BYTES, tm, &bars->k_full[s], p.E + kc.I.h * HD,
+                    kc.j * BN, kc.I.b);
+        last_k[s] = kc.g;
+        kc.advance(p);
+        if (vc.g + 1 < kc.g && !(ok = load_v())) break;  // V one tile behind K
     }
-    if (!ok) raise_abort(bars, p.status, ST_PREFILL_LOAD_TIMEOUT);
+    while (ok && vc.valid && !aborted(bars)) ok = load_v();  // the remaining V tiles
+    if (!ok && !aborted(bars)) raise_abort(bars, p.status, ST_PREFILL_LOAD_TIMEOUT);
     // Teardown guard: every copy this thread issued must have landed before the CTA exits.
-    bool drained = mbar_wait(&bars->q_full, 0, to);
-    for (int st = 0; st < NSTAGE; ++st) {
-        if (last_issue[st] < 0) continue;
-        const uint32_t par = (last_issue[st] / NSTAGE) & 1;
-        drained = mbar_wait(&bars->k_full[st], par, to) && drained;
-        drained = mbar_wait(&bars->v_full[st], par, to) && drained;
+    bool drained = true;
+    for (int s = 0; s < NQ; ++s)
+        if (last_q[s] >= 0) drained = mbar_wait(&bars->q_full[s], (last_q[s] / NQ) & 1, to) && drained;
+    for (int s = 0; s < NSTAGE; ++s) {
+        if (last_k[s] >= 0) drained = mbar_wait(&bars->k_full[s], (last_k[s] / NSTAGE) & 1, to) && drained;
+        if (last_v[s] >= 0) drained = mbar_wait(&bars->v_full[s], (last_v[s] / NSTAGE) & 1, to) && drained;
     }
     if (!drained) atomicOr(p.status, ST_PREFILL_DRAIN_TIMEOUT);
 }
 
-// ------------------------------------------------------------------ MMA issuer (one thread)
-__device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int nk) {
+// ------------------------------------------------------------------ MMA issuers (one thread per query tile)
+// Each query tile x has its own issuing thread, so neither stream's MMAs queue behind the other's
+// dependencies. Both walk every K/V tile of every item; the shared K, V and Q stages are released
+// through two-arrival barriers: a stream commits its MMAs on them (or, for a tile it does not use,
+// arrives after that tile has landed, so that arrivals of different phases cannot mix).
+__device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int x) {
     const unsigned long long to = p.timeout_ns;
-    const uint32_t tS = tbase + TCOL_S, tO = tbase + TCOL_O;
-    const uint32_t aQ = smem_u32(smem + OFF_Q);
-    const uint32_t aK = smem_u32(smem + OFF_K);
-    const uint32_t aV = smem_u32(smem + OFF_V);
-    const uint32_t aP = smem_u32(smem + OFF_P);
+    Stream &S = bars->st[x];
+    // Descriptors are built once; an MMA then only adds a K-step offset to the start-address word
+    // (+32 B per K16 step inside a 128-byte swizzled row, +2 KB = 16 rows of V per K16 step).
+    const uint64_t dq0 = sdesc_sw128(smem_u32(smem + OFF_Q), 16, 1024);
+    const uint64_t dk0 = sdesc_sw128(smem_u32(smem + OFF_K), 16, 1024);
+    const uint64_t dv0 = sdesc_sw128(smem_u32(smem + OFF_V), TILE_BYTES, 1024);
+    const uint32_t q_lo = static_cast<uint32_t>(dq0), q_hi = static_cast<uint32_t>(dq0 >> 32);
+    const uint32_t k_lo = static_cast<uint32_t>(dk0), k_hi = static_cast<uint32_t>(dk0 >> 32);
+    const uint32_t v_lo = static_cast<uint32_t>(dv0), v_hi = static_cast<uint32_t>(dv0 >> 32);
+    constexpr uint32_t TILE_DESC = TILE_BYTES >> 4;  // one 16 KB tile in start-address units
+    const uint32_t tS = tbase + TCOL_S + 128 * x, tO = tbase + TCOL_O + 64 * x;
+    const uint32_t tP = tbase + TCOL_P + 64 * x;
 
-    auto issue_qk = [&](int st) {
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t da = sdesc_sw128(aQ + kk * 32, 16, 1024);
-            const uint64_t db = sdesc_sw128(aK + st * TILE_BYTES + kk * 32, 16, 1024);
-            umma_f16_ss(tS, da, db, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-    };
-    auto issue_pv = [&](int st, bool first) {
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t da = sdesc_sw128(aP + (kk >> 2) * P_BLOCK_BYTES + (kk & 3) * 32, 16, 1024);
-            const uint64_t db = sdesc_sw128(aV + st * TILE_BYTES + kk * 2048, TILE_BYTES, 1024);
-            umma_f16_ss(tO, da, db, IDESC_O, (first && kk == 0) ? 0u : 1u);
-        }
-    };
-
-    bool ok = mbar_wait(&bars->q_full, 0, to) && mbar_wait(&bars->k_full[0], 0, to);
-    if (ok) {
-        tc_fence_after();
-        issue_qk(0);
-        umma_commit(&bars->s_full);
-    }
-    for (int j = 0; ok && j < nk; ++j) {
-        if (j + 1 < nk) {
-            const int st1 = (j + 1) % NSTAGE;
-            ok = mbar_wait(&bars->k_full[st1], ((j + 1) / NSTAGE) & 1, to) &&
-                 mbar_wait(&bars->s_free, j & 1, to);
-            if (!ok) break;
+    int gs = 0;   // this query tile's QKs issued (all items)
+    int gp = 0;   // this query tile's PVs issued
+    int itp = 0;  // items in which this query tile's PVs have started (for o_free)
+    // S = Q K^T for the K/V tile under cursor q (or release of that tile if this query tile skips it).
+    auto qk_step = [&](const Cursor &q) -> bool {
+        const int qb = q.it % NQ, s = q.g % NSTAGE;
+        const bool uses = q.j < q.I.nk[x];
+        if (q.j == 0 && !mbar_wait(&bars->q_full[qb], (q.it / NQ) & 1, to)) return false;
+        if (!mbar_wait(&bars->k_full[s], (q.g / NSTAGE) & 1, to)) return false;
+        if (uses) {
+            if (gs > 0 && !mbar_wait(&S.s_free, (gs - 1) & 1, to)) return false;
             tc_fence_after();
-            issue_qk(st1);
-            umma_commit(&bars->s_full);
+            const uint32_t a = q_lo + (qb * 2 + x) * TILE_DESC, b = k_lo + s * TILE_DESC;
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk)
+                umma_f16_ss_lohi(tS, a + 2 * kk, q_hi, b + 2 * kk, k_hi, IDESC_S, kk > 0 ? 1u : 0u);
+            umma_commit(&S.s_full);
+            umma_commit(&bars->k_empty[s]);
+            ++gs;
+        } else {
+            mbar_arrive(&bars->k_empty[s]);
         }
-        const int st = j % NSTAGE;
-        ok = mbar_wait(&bars->p_full, j & 1, to) && mbar_wait(&bars->v_full[st], (j / NSTAGE) & 1, to);
-        if (!ok) break;
+        // the Q buffer: released after this stream's last QK of the item (or at once if it has none)
+        const int last = q.I.nk[x] ? q.I.nk[x] - 1 : 0;
+        if (q.j == last) {
+            if (uses) umma_commit(&bars->q_empty[qb]);
+            else mbar_arrive(&bars->q_empty[qb]);
+        }
+        return true;
+    };
+    // O += P V for the K/V tile under cursor v (or release of that tile).
+    auto pv_step = [&](const Cursor &v) -> bool {
+        const int s = v.g % NSTAGE;
+        if (!mbar_wait(&bars->v_full[s], (v.g / NSTAGE) & 1, to)) return false;
+        if (v.j >= v.I.nk[x]) {
+            mbar_arrive(&bars->v_empty[s]);
+            return true;
+        }
+        if (!mbar_wait(&S.p_full, gp & 1, to)) return false;
+        if (v.j == 0) {
+            if (itp > 0 && !mbar_wait(&S.o_free, (itp - 1) & 1, to)) return false;
+            ++itp;
+        }
         tc_fence_after();
-        issue_pv(st, j == 0);
-        umma_commit(&bars->o_done);
-        umma_commit(&bars->kv_empty[st]);
+        const uint32_t b = v_lo + s * TILE_DESC;
+        umma_f16_ts_lohi(tO, tP, b, v_hi, IDESC_O, v.j == 0 ? 0u : 1u);
+#pragma unroll
+        for (int kk = 1; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P per step
+            umma_f16_ts_lohi(tO, tP + kk * 8, b + 128 * kk, v_hi, IDESC_O, 1u);
+        umma_commit(&S.o_done);
+        umma_commit(&bars->v_empty[s]);
+        ++gp;
+        return true;
+    };
+
+    Cursor q, v;  // q: next K/V tile for QK; v: next tile for PV (one behind q)
+    q.start(p);
+    v.start(p);
+    bool ok = true;
+    if (q.valid) {
+        ok = qk_step(q);
+        q.advance(p);
+    }
+    while (ok && v.valid) {
+        if (q.valid) {
+            ok = qk_step(q);
+            if (!ok) break;
+            q.advance(p);
+        }
+        ok = pv_step(v);
+        if (!ok) break;
+        v.advance(p);
     }
     if (!ok) raise_abort(bars, p.status, ST_PREFILL_MMA_TIMEOUT);
     // Teardown guard: all MMAs issued by this thread complete before TMEM is released.
-    umma_commit(&bars->drain);
-    if (!mbar_wait(&bars->drain, 0, to)) atomicOr(p.status, ST_PREFILL_DRAIN_TIMEOUT);
+    umma_commit(&S.drain);
+    if (!mbar_wait(&S.drain, 0, to)) atomicOr(p.status, ST_PREFILL_DRAIN_TIMEOUT);
 }
 
-// ------------------------------------------------------------------ softmax + epilogue (4 warps)
+// ------------------------------------------------------------------ softmax + epilogue
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
                                           unsigned long long to) {
     const bool ok = mbar_wait(bar, parity, to);
     return __all_sync(0xffffffffu, ok);
 }
 
-__device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int warp,
-                            int lane, int b, int h, int qt, int nk) {
+// Softmax of query tile x (0 = A, 1 = B) of every item: 4 warps, thread = one query row (TMEM lane),
+// all 128 scores of a tile in registers.
+__device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int x,
+                            int warp, int lane) {
     const unsigned long long to = p.timeout_ns;
-    const int quarter = warp & 3;              // TMEM lane quarter this warp may access
-    const int r = quarter * 32 + lane;         // query row within the tile
+    Stream &S = bars->st[x];
+    Stream &O = bars->st[x ^ 1];  // the other query tile
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access (= SM sub-partition)
+    const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t tl = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t tS = tl + TCOL_S, tO = tl + TCOL_O;
+    const uint32_t tS = tl + TCOL_S + 128 * x;
+    const uint32_t tO = tl + TCOL_O + 64 * x;
+    const uint32_t tP = tl + TCOL_P + 64 * x;
     const float c = p.scale_log2;
-    uint8_t *sP = smem + OFF_P;
 
-    float m_used = -INFINITY;  // running max (log2 units) used for the exponentials
-    float l = 0.f;             // running sum of exponentials
+    int g = 0;  // this query tile's K/V tiles processed so far (all items)
+    // Ping-pong on the MUFU: the ex2 loops of the A warp and the B warp that share an SM
+    // sub-partition alternate, in the order A0 B0 A1 B1 ... of each item (B's extra diagonal tile
+    // follows its own previous one). ocum = ex2 phases the other query tile completed in earlier
+    // items; before our phase k of an item we wait until the other tile's warp on this sub-partition
+    // has completed ocum + min(k + x, nk_other) phases (x = 0 for A, 1 for B). The counts are
+    // monotonic shared-memory counters (a parity barrier would alias: at an item boundary B runs two
+    // phases in a row, so A may need a count two ahead of the current one).
+    int ocum = 0;
+    int ex2_phases = 0;  // this warp's completed ex2 phases
     bool ok = true;
-
-    for (int j = 0; j < nk; ++j) {
-        ok = warp_wait(&bars->s_full, j & 1, to);
-        if (!ok) break;
-        tc_fence_after();
-        float x[BN];
-#pragma unroll
-        for (int cb = 0; cb < BN / 32; ++cb) {
-            uint32_t v[32];
-            tmem_ld32(tS + cb * 32, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) x[cb * 32 + i] = __uint_as_float(v[i]);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->s_free);
-
-        if (j == nk - 1) {  // diagonal tile (BM == BN): key c of this tile is visible iff c <= r
-#pragma unroll
-            for (int i = 0; i < BN; ++i)
-                if (i > r) x[i] = -INFINITY;
-        }
-        float pm[8];  // 8 independent partial maxima (no 127-long dependency chain)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) pm[k] = x[k];
-#pragma unroll
-        for (int i = 8; i < BN; ++i) pm[i & 7] = fmaxf(pm[i & 7], x[i]);
-        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-        const float mt = mx * c;
-        float alpha = 1.f;
-        bool resc = false;
-        if (mt > m_used + RESCALE_THRESHOLD) {
-            alpha = ex2_approx(m_used - mt);  // 0 on the first tile (m_used = -inf)
-            m_used = mt;
-            l *= alpha;
-            resc = true;
-        }
-        const float neg_m = -m_used;
-        uint32_t pk[BN / 2];
-        // The row sum adds the fp16-ROUNDED p values (the ones the PV MMA consumes), so numerator
-        // and denominator see the same weights; 8 independent partial sums keep the adds parallel.
-        float ps[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) ps[k] = 0.f;
-#pragma unroll
-        for (int i = 0; i < BN / 2; ++i) {
-            const float p0 = ex2_approx(fmaf(x[2 * i], c, neg_m));
-            const float p1 = ex2_approx(fmaf(x[2 * i + 1], c, neg_m));
-            pk[i] = pack_half2(p0, p1);
-            ps[(2 * i) & 7] = add_f16lo_f32(pk[i], ps[(2 * i) & 7]);
-            ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[i], ps[(2 * i + 1) & 7]);
-        }
-        l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-
-        if (j > 0) {  // PV_{j-1} must be done: it reads the P buffer and writes O
-            ok = warp_wait(&bars->o_done, (j - 1) & 1, to);
+    Item I;
+    for (int it = 0; ok && get_item(p, it, I); ocum += I.nk[x ^ 1], ++it) {
+        const int nk = I.nk[x];
+        if (nk == 0) continue;     // no tile B in this item
+        float m_used = -INFINITY;  // running max (log2 units) used for the exponentials
+        float l = 0.f;             // running sum of the (fp16-rounded) exponentials
+        for (int j = 0; j < nk; ++j, ++g) {
+            ok = warp_wait(&S.s_full, g & 1, to);
             if (!ok) break;
             tc_fence_after();
-        }
-        // P row r -> two K-major SW128 blocks (keys 0-63, 64-127); 16-byte chunk g of the row lands
-        // at chunk position (g ^ (r & 7)) of its 128-byte row, as TMA would have placed it.
+            float xs[BN];
+            {
+                uint32_t v[4][32];
 #pragma unroll
-        for (int g = 0; g < BN / 8; ++g) {
-            uint8_t *dst = sP + (g >> 3) * P_BLOCK_BYTES + r * 128 + (((g & 7) ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4 *>(dst) =
-                make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-        }
-        if (j > 0 && __any_sync(0xffffffffu, resc)) {
-#pragma unroll
-            for (int cb = 0; cb < HD / 32; ++cb) {
-                uint32_t v[32];
-                tmem_ld32(tO + cb * 32, v);
+                for (int cb = 0; cb < 4; ++cb) tmem_ld32(tS + 32 * cb, v[cb]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-                tmem_st32(tO + cb * 32, v);
+                for (int cb = 0; cb < 4; ++cb)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) xs[32 * cb + i] = __uint_as_float(v[cb][i]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.s_free);  // the next QK may overwrite S
+
+            if (j == nk - 1) {  // diagonal tile (BM == BN): key k is visible iff k <= r
+#pragma unroll
+                for (int i = 0; i < BN; ++i)
+                    if (i > r) xs[i] = -INFINITY;
+            }
+            float pm[8];  // independent partial maxima, three-input max
+#pragma unroll
+            for (int k = 0; k < 8; ++k) pm[k] = fmaxf(xs[k], xs[8 + k]);
+#pragma unroll
+            for (int i = 16; i < BN; i += 16)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) pm[k] = max3f(pm[k], xs[i + k], xs[i + 8 + k]);
+            const float mt = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]),
+                                   fmaxf(pm[6], pm[7])) * c;
+            float alpha = 1.f;
+            bool resc = false;
+            if (mt > m_used + RESCALE_THRESHOLD) {
+                alpha = ex2_approx(m_used - mt);  // 0 on the first tile (m_used = -inf)
+                m_used = mt;
+                l *= alpha;
+                resc = true;
+            }
+            const float neg_m = -m_used;
+            if (g > 0) {  // the previous PV of this query tile is done: P may be overwritten and O
+                          // holds its result
+                ok = warp_wait(&S.o_done, (g - 1) & 1, to);
+                if (!ok) break;
+                tc_fence_after();
+            }
+            {  // wait for our turn on this sub-partition's MUFU (time-bounded spin on the counter)
+                const int need = ocum + min(j + x, I.nk[x ^ 1]);
+                int ready = 1;
+                if (lane == 0 && need > 0) {
+                    const volatile int *cnt = &O.ex2_done[quarter];
+                    uint64_t t0 = 0;
+                    for (int spin = 0;; ++spin) {
+                        if (*cnt >= need) break;
+                        if (spin == 32) t0 = globaltimer_ns();
+                        if (spin > 32) {
+                            if (globaltimer_ns() - t0 > to) {
+                                ready = 0;
+                                break;
+                            }
+                            __nanosleep(32);
+                        }
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ready, 0) != 0;
+                if (!ok) break;
+            }
+            // P = 2^(s - m) as packed fp16, 32 keys at a time straight into TMEM. The row sum adds the
+            // fp16-ROUNDED values (the ones the PV MMA consumes).
+            float ps[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ps[k] = 0.f;
+#pragma unroll
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = ex2_approx(fmaf(xs[32 * cb + 2 * i], c, neg_m));
+                    const float p1 = ex2_approx(fmaf(xs[32 * cb + 2 * i + 1], c, neg_m));
+                    pk[i] = pack_half2(p0, p1);
+                    ps[(2 * i) & 7] = add_f16lo_f32(pk[i], ps[(2 * i) & 7]);
+                    ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[i], ps[(2 * i + 1) & 7]);
+                }
+                tmem_st16(tP + 16 * cb, pk);
+            }
+            l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            __syncwarp();
+            ++ex2_phases;
+            if (lane == 0)  // the other query tile's warp on this sub-partition may go
+                *reinterpret_cast<volatile int *>(&S.ex2_done[quarter]) = ex2_phases;
+            if (j > 0 && __any_sync(0xffffffffu, resc)) {
+#pragma unroll
+                for (int cb = 0; cb < 2; ++cb) {
+                    uint32_t v[32];
+                    tmem_ld32(tO + 32 * cb, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                    tmem_st32(tO + 32 * cb, v);
+                }
             }
             tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.p_full);
         }
-        fence_proxy_async_smem();
+        if (!ok) break;
+        // ---- epilogue of this item
+        ok = warp_wait(&S.o_done, (g - 1) & 1, to);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t v[2][32];
+        tmem_ld32(tO, v[0]);
+        tmem_ld32(tO + 32, v[1]);
+        tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_full);
-    }
-    if (!ok) {
-        raise_abort(bars, p.status, ST_PREFILL_SOFTMAX_TIMEOUT);
-        return;
-    }
-    ok = warp_wait(&bars->o_done, (nk - 1) & 1, to);
-    if (!ok) {
-        raise_abort(bars, p.status, ST_PREFILL_SOFTMAX_TIMEOUT);
-        return;
-    }
-    tc_fence_after();
-    const float inv_l = 1.f / l;
-    const int row = qt * BM + r;
-    __half *dst = p.att + static_cast<long long>(b) * p.att_seq_stride +
-                  static_cast<long long>(row) * p.E + h * HD;
-#pragma unroll
-    for (int cb = 0; cb < HD / 32; ++cb) {
-        uint32_t v[32];
-        tmem_ld32(tO + cb * 32, v);
-        tmem_wait_ld();
-        uint32_t o[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-            o[i] = pack_half2(__uint_as_float(v[2 * i]) * inv_l, __uint_as_float(v[2 * i + 1]) * inv_l);
+        if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
+        const float inv_l = 1.f / l;
+        const int row = (2 * I.pair + x) * BM + r;
         if (row < p.T) {
-            uint4 *d4 = reinterpret_cast<uint4 *>(dst + cb * 32);
+            __half *dst = p.att + static_cast<long long>(I.b) * p.att_seq_stride +
+                          static_cast<long long>(row) * p.E + I.h * HD;
+            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) d4[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            for (int cb = 0; cb < 2; ++cb) {
+                uint32_t o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    o[i] = pack_half2(__uint_as_float(v[cb][2 * i]) * inv_l,
+                                      __uint_as_float(v[cb][2 * i + 1]) * inv_l);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    d4[4 * cb + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            }
         }
     }
+    if (!ok) raise_abort(bars, p.status, ST_PREFILL_SOFTMAX_TIMEOUT);
 }
 
-__global__ void __launch_bounds__(NTHREADS, 2)
+__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    // Heaviest tiles first: item i -> query tile (n_qtiles-1 - i / (H*B)), then head, then sequence.
-    const int per = p.H * p.B;
-    const int item = blockIdx.x;
-    const int qt = p.n_qtiles - 1 - item / per;
-    const int rem = item % per;
-    const int h = rem % p.H;
-    const int b = rem / p.H;
-    const int nk = qt + 1;  // causal: KV tiles 0..qt
 
     if ((smem_u32(smem) & 1023u) != 0) {  // SW128 tiles need 1024-byte alignment; uniform exit
         if (threadIdx.x == 0) atomicOr(p.status, ST_PREFILL_SMEM_ALIGN);
         return;
     }
     if (threadIdx.x == 0) {
-        mbar_init(&bars->q_full, 1);
+        for (int s = 0; s < NQ; ++s) {
+            mbar_init(&bars->q_full[s], 1);
+            mbar_init(&bars->q_empty[s], 2);
+        }
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&bars->k_full[s], 1);
+            mbar_init(&bars->k_empty[s], 2);  // one release per query tile
             mbar_init(&bars->v_full[s], 1);
-            mbar_init(&bars->kv_empty[s], 1);
+            mbar_init(&bars->v_empty[s], 2);
         }
-        mbar_init(&bars->s_full, 1);
-        mbar_init(&bars->s_free, 4);
-        mbar_init(&bars->p_full, 4);
-        mbar_init(&bars->o_done, 1);
-        mbar_init(&bars->drain, 1);
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&bars->st[x].s_full, 1);
+            mbar_init(&bars->st[x].s_free, NSOFT_WARPS);
+            mbar_init(&bars->st[x].p_full, NSOFT_WARPS);
+            mbar_init(&bars->st[x].o_done, 1);
+            mbar_init(&bars->st[x].o_free, NSOFT_WARPS);
+            mbar_init(&bars->st[x].drain, 1);
+            for (int q = 0; q < 4; ++q) bars->st[x].ex2_done[q] = 0;
+        }
         bars->abort = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
@@ -356,13 +540,13 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     const uint32_t tbase = bars->tmem_base;
 
     if (warp == 0) {
-        if (lane == 0) run_producer(&tm_qkv, smem, bars, p, b, h, qt, nk);
+        if (lane == 0) run_producer(&tm_qkv, smem, bars, p);
         __syncwarp();
-    } else if (warp == 1) {
-        if (lane == 0) run_mma(smem, bars, p, tbase, nk);
+    } else if (warp == 1 || warp == MMA_B_WARP) {
+        if (lane == 0) run_mma(smem, bars, p, tbase, warp == 1 ? 0 : 1);
         __syncwarp();
     } else {
-        run_softmax(smem, bars, p, tbase, warp, lane, b, h, qt, nk);
+        run_softmax(smem, bars, p, tbase, (warp - 2) / NSOFT_WARPS, warp, lane);
     }
 
     tc_fence_before();
@@ -432,13 +616,18 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     p.E = E;
     p.B = B;
     p.n_qtiles = (T + BM - 1) / BM;
+    p.n_pairs = (p.n_qtiles + 1) / 2;
+    const long long total = static_cast<long long>(p.n_pairs) * H * B;
+    if (total <= 0) return GPT2_B200_OK;
+    if (total > 0x7fffffffLL) return GPT2_B200_EINVAL;
+    p.total_items = static_cast<int>(total);
     p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(HD)));
     p.status = ctx->status;
     p.timeout_ns = wait_timeout_ns();
-    const long long grid = static_cast<long long>(p.n_qtiles) * H * B;
-    if (grid <= 0) return GPT2_B200_OK;
-    if (grid > 0x7fffffffLL) return GPT2_B200_EINVAL;
-    k_flash_prefill_tc<<<static_cast<unsigned>(grid), NTHREADS, SMEM_BYTES, stream>>>(tm, p);
+    // Persistent: at most CTAS_PER_SM resident CTAs per SM, each looping over its share of items.
+    const long long slots = static_cast<long long>(CTAS_PER_SM) * (ctx->num_sms > 0 ? ctx->num_sms : 148);
+    const unsigned grid = static_cast<unsigned>(total < slots ? total : slots);
+    k_flash_prefill_tc<<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, p);
     return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 
