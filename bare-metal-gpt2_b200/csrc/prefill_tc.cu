@@ -16,24 +16,25 @@
 //   warp 0   (1 thread)  TMA producer: the two Q tiles of each item (double-buffered), then K(t) and
 //                        V(t-1) tiles (128 x 64 fp16, 128-byte swizzle) straight out of the packed qkv
 //                        rows into 4-stage K and V rings, running ahead across item boundaries.
-//   warps 1, 18 (1 thr)  MMA issuers, one per query tile x: per K/V tile, S_x = Q_x K^T (M128 N128 K64,
+//   warps 1, 10 (1 thr)  MMA issuers, one per query tile x: per K/V tile, S_x = Q_x K^T (M128 N128 K64,
 //                        4 x tcgen05.mma K16, operands in shared memory), then O_x += P_x V (M128 N64
 //                        K128, 8 x tcgen05.mma K16, P read from TMEM). Two independent issue streams
 //                        and four accumulators keep the tensor pipe busy; shared-memory descriptors are
 //                        built once and advanced by 32-bit adds.
-//   warps 2-9, 10-17     softmax of query tile A, of query tile B: TMEM lane r = query row r; each
-//                        row's 128 scores are split between two warps (keys 0-63 / 64-127) that
-//                        exchange their partial maxima through shared memory and a two-arrival
-//                        mbarrier. Log2 domain (1/8 * log2(e) folded into one FFMA, hardware ex2);
-//                        causal mask on the diagonal tile only; P = 2^(s-m) written as packed fp16
-//                        straight into TMEM (one tcgen05.st per thread); the row sum adds the
-//                        fp16-rounded P values (numerator and denominator use identical weights); O is
-//                        rescaled in TMEM only when the running max grows by more than 2^8 (the stale
-//                        max is otherwise kept for both l and O: exact, and P <= 256). Epilogue:
-//                        O / l -> fp16 -> att, then O is released for the next item.
+//   warps 2-5, 6-9       softmax of query tile A, of query tile B: one thread per query row (TMEM lane),
+//                        all 128 scores of a tile in registers. Log2 domain (1/8 * log2(e) folded into
+//                        one FFMA, hardware ex2); causal mask on the diagonal tile only; P = 2^(s-m)
+//                        written as packed fp16 straight into TMEM; the row sum adds the fp16-rounded
+//                        P values (numerator and denominator use identical weights); O is rescaled in
+//                        TMEM only when the running max grows by more than 2^8 (the stale max is
+//                        otherwise kept for both l and O: exact, and P <= 256). The A and B warps that
+//                        share an SM sub-partition take turns on its MUFU (ex2) pipe. Epilogue: O / l ->
+//                        fp16 -> a swizzled 4 KB shared-memory slot per warp -> one TMA store of the
+//                        warp's 32 rows, so output rows leave as whole 128-byte lines.
 //
-// TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 196 KB.
-// No cluster, no multicast. Every mbarrier wait is bounded.
+// TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 224.5 KB
+// (Q 64 KB, K and V rings 128 KB, output slots 32 KB, barriers). No cluster, no multicast. Every
+// mbarrier wait is bounded.
 #include <cmath>
 #include <cstdio>
 
@@ -52,8 +53,12 @@ constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB: 128 rows x 128 B
 constexpr int OFF_Q = 0;                                     // [NQ][2 tiles]
 constexpr int OFF_K = OFF_Q + NQ * 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + NSTAGE * TILE_BYTES;
-constexpr int OFF_BAR = OFF_V + NSTAGE * TILE_BYTES;
+constexpr int OUT_ROWS = 32;                    // output rows per softmax warp (one TMA store box)
+constexpr int OUT_SLOT = OUT_ROWS * HD * 2;     // 4 KB: 32 rows x 128 B, 128-byte swizzle
+constexpr int OFF_OUT = OFF_V + NSTAGE * TILE_BYTES;  // [2 query tiles][4 warps] output slots
+constexpr int OFF_BAR = OFF_OUT + 2 * 4 * OUT_SLOT;
 constexpr int SMEM_BYTES = OFF_BAR + 512;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 constexpr int NSOFT_WARPS = 4;  // per query tile: one warp per TMEM lane quarter
 constexpr int NTHREADS = 32 * (3 + 2 * NSOFT_WARPS);  // producer, 2 MMA issuers, 2 softmax groups
 constexpr int MMA_B_WARP = 2 + 2 * NSOFT_WARPS;              // warp 10 issues query tile B's MMAs
@@ -90,8 +95,6 @@ struct __align__(8) Bars {
 static_assert(sizeof(Bars) <= 512, "barrier block");
 
 struct Params {
-    __half *att;
-    long long att_seq_stride;  // elements between sequences of att
     int T, H, E, B;
     int n_qtiles;
     int n_pairs;               // ceil(n_qtiles / 2)
@@ -105,6 +108,8 @@ struct Item {
     int pair, h, b;
     int nk[2];  // K/V tiles of query tile A (2p+1) and of B (2p+2, or 0 when tile 2p+1 is past T)
     int nkv;    // K/V tiles loaded for the item: max(nk)
+    // nk[x] for a runtime x without a local-memory array access
+    __device__ __forceinline__ int nk_of(int x) const { return x ? nk[1] : nk[0]; }
 };
 
 // The r-th item of this CTA. Items are numbered heaviest first (the last pair of every head and
@@ -242,7 +247,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
     // S = Q K^T for the K/V tile under cursor q (or release of that tile if this query tile skips it).
     auto qk_step = [&](const Cursor &q) -> bool {
         const int qb = q.it % NQ, s = q.g % NSTAGE;
-        const bool uses = q.j < q.I.nk[x];
+        const bool uses = q.j < q.I.nk_of(x);
         if (q.j == 0 && !mbar_wait(&bars->q_full[qb], (q.it / NQ) & 1, to)) return false;
         if (!mbar_wait(&bars->k_full[s], (q.g / NSTAGE) & 1, to)) return false;
         if (uses) {
@@ -259,7 +264,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
             mbar_arrive(&bars->k_empty[s]);
         }
         // the Q buffer: released after this stream's last QK of the item (or at once if it has none)
-        const int last = q.I.nk[x] ? q.I.nk[x] - 1 : 0;
+        const int last = q.I.nk_of(x) ? q.I.nk_of(x) - 1 : 0;
         if (q.j == last) {
             if (uses) umma_commit(&bars->q_empty[qb]);
             else mbar_arrive(&bars->q_empty[qb]);
@@ -270,7 +275,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
     auto pv_step = [&](const Cursor &v) -> bool {
         const int s = v.g % NSTAGE;
         if (!mbar_wait(&bars->v_full[s], (v.g / NSTAGE) & 1, to)) return false;
-        if (v.j >= v.I.nk[x]) {
+        if (v.j >= v.I.nk_of(x)) {
             mbar_arrive(&bars->v_empty[s]);
             return true;
         }
@@ -324,13 +329,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
 
 // Softmax of query tile x (0 = A, 1 = B) of every item: 4 warps, thread = one query row (TMEM lane),
 // all 128 scores of a tile in registers.
-__device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int x,
-                            int warp, int lane) {
+__device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CUtensorMap *tm_att,
+                            uint32_t tbase, int x, int warp, int lane) {
     const unsigned long long to = p.timeout_ns;
     Stream &S = bars->st[x];
     Stream &O = bars->st[x ^ 1];  // the other query tile
-    const int quarter = warp & 3;       // TMEM lane quarter this warp may access (= SM sub-partition)
-    const int r = quarter * 32 + lane;  // query row within the tile
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access (= SM sub-partition)
     const uint32_t tl = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t tS = tl + TCOL_S + 128 * x;
     const uint32_t tO = tl + TCOL_O + 64 * x;
@@ -344,13 +348,14 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
     // items; before our phase k of an item we wait until the other tile's warp on this sub-partition
     // has completed ocum + min(k + x, nk_other) phases (x = 0 for A, 1 for B). The counts are
     // monotonic shared-memory counters (a parity barrier would alias: at an item boundary B runs two
-    // phases in a row, so A may need a count two ahead of the current one).
+    // phases in a row, so A may need a count two ahead of the current one). They only order work;
+    // no data passes through them.
     int ocum = 0;
     int ex2_phases = 0;  // this warp's completed ex2 phases
     bool ok = true;
     Item I;
-    for (int it = 0; ok && get_item(p, it, I); ocum += I.nk[x ^ 1], ++it) {
-        const int nk = I.nk[x];
+    for (int it = 0; ok && get_item(p, it, I); ocum += I.nk_of(x ^ 1), ++it) {
+        const int nk = I.nk_of(x);
         if (nk == 0) continue;     // no tile B in this item
         float m_used = -INFINITY;  // running max (log2 units) used for the exponentials
         float l = 0.f;             // running sum of the (fp16-rounded) exponentials
@@ -374,6 +379,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
             if (lane == 0) mbar_arrive(&S.s_free);  // the next QK may overwrite S
 
             if (j == nk - 1) {  // diagonal tile (BM == BN): key k is visible iff k <= r
+                const int r = quarter * 32 + lane;
 #pragma unroll
                 for (int i = 0; i < BN; ++i)
                     if (i > r) xs[i] = -INFINITY;
@@ -403,7 +409,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
                 tc_fence_after();
             }
             {  // wait for our turn on this sub-partition's MUFU (time-bounded spin on the counter)
-                const int need = ocum + min(j + x, I.nk[x ^ 1]);
+                const int need = ocum + min(j + x, I.nk_of(x ^ 1));
                 int ready = 1;
                 if (lane == 0 && need > 0) {
                     const volatile int *cnt = &O.ex2_done[quarter];
@@ -428,9 +434,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
             float ps[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) ps[k] = 0.f;
-#pragma unroll
-            for (int cb = 0; cb < 4; ++cb) {
-                uint32_t pk[16];
+            auto exp_chunk = [&](const int cb, uint32_t(&pk)[16]) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const float p0 = ex2_approx(fmaf(xs[32 * cb + 2 * i], c, neg_m));
@@ -439,6 +443,11 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
                     ps[(2 * i) & 7] = add_f16lo_f32(pk[i], ps[(2 * i) & 7]);
                     ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[i], ps[(2 * i + 1) & 7]);
                 }
+            };
+#pragma unroll
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t pk[16];
+                exp_chunk(cb, pk);
                 tmem_st16(tP + 16 * cb, pk);
             }
             l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
@@ -463,41 +472,58 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
             if (lane == 0) mbar_arrive(&S.p_full);
         }
         if (!ok) break;
-        // ---- epilogue of this item
+        // ---- epilogue of this item: O / l -> fp16 -> this warp's output slot -> one TMA store of
+        // its 32 rows (rows past T are clipped by the tensor map)
         ok = warp_wait(&S.o_done, (g - 1) & 1, to);
         if (!ok) break;
         tc_fence_after();
-        uint32_t v[2][32];
-        tmem_ld32(tO, v[0]);
-        tmem_ld32(tO + 32, v[1]);
-        tmem_wait_ld();
-        tc_fence_before();
+        // the slot's previous store has finished reading it (returns at once if none is pending)
+        if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
-        const float inv_l = 1.f / l;
-        const int row = (2 * I.pair + x) * BM + r;
-        if (row < p.T) {
-            __half *dst = p.att + static_cast<long long>(I.b) * p.att_seq_stride +
-                          static_cast<long long>(row) * p.E + I.h * HD;
-            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+        {
+            const float inv_l = 1.f / l;
+            // This warp's output slot: its 32 rows x 64 columns, row `lane` at lane * 128 B, 16-byte
+            // chunk k of a row at chunk position k ^ (row % 8) (the TMA 128-byte swizzle, which also
+            // makes these writes bank-conflict-free).
+            uint8_t *my_row = smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT + lane * (HD * 2);
 #pragma unroll
-            for (int cb = 0; cb < 2; ++cb) {
+            for (int cb = 0; cb < 2; ++cb) {  // 32 columns of O at a time
+                uint32_t v[32];
+                tmem_ld32(tO + 32 * cb, v);
+                tmem_wait_ld();
                 uint32_t o[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
-                    o[i] = pack_half2(__uint_as_float(v[cb][2 * i]) * inv_l,
-                                      __uint_as_float(v[cb][2 * i + 1]) * inv_l);
+                    o[i] = pack_half2(__uint_as_float(v[2 * i]) * inv_l,
+                                      __uint_as_float(v[2 * i + 1]) * inv_l);
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    d4[4 * cb + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                for (int q = 0; q < 4; ++q) {
+                    const int chunk = (4 * cb + q) ^ (lane & 7);
+                    *reinterpret_cast<uint4 *>(my_row + chunk * 16) =
+                        make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                }
             }
+        }
+        tc_fence_before();
+        fence_proxy_async_smem();  // this thread's slot writes -> visible to the TMA engine
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
+        const int row0 = (2 * I.pair + x) * BM + quarter * OUT_ROWS;
+        if (lane == 0 && row0 < p.T) {  // rows past T inside the box are clipped by the tensor map
+            tma_store_3d(tm_att, smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT, I.h * HD, row0, I.b);
+            bulk_commit_group();
         }
     }
     if (!ok) raise_abort(bars, p.status, ST_PREFILL_SOFTMAX_TIMEOUT);
+    // The CTA's shared memory must outlive the stores that read it, and the launch ends with the
+    // output written.
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
 }
 
 __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
-    k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv, const Params p) {
+    k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv,
+                       const __grid_constant__ CUtensorMap tm_att, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -529,6 +555,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         bars->abort = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
+        tma_prefetch_desc(&tm_att);
     }
     if (warp == 1) {
         tmem_alloc(&bars->tmem_base, TMEM_COLS);
@@ -546,7 +573,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         if (lane == 0) run_mma(smem, bars, p, tbase, warp == 1 ? 0 : 1);
         __syncwarp();
     } else {
-        run_softmax(smem, bars, p, tbase, (warp - 2) / NSOFT_WARPS, warp, lane);
+        run_softmax(smem, bars, p, &tm_att, tbase, (warp - 2) / NSOFT_WARPS, warp, lane);
     }
 
     tc_fence_before();
@@ -607,10 +634,19 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return GPT2_B200_EINVAL;
+    // att [B][T][E] (sequence stride att_seq_stride): one store box = 32 rows x 64 columns of a head
+    CUtensorMap tm_att;
+    const cuuint64_t odims[3] = {static_cast<cuuint64_t>(E), static_cast<cuuint64_t>(T),
+                                 static_cast<cuuint64_t>(B)};
+    const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(E) * 2,
+                                    static_cast<cuuint64_t>(att_seq_stride) * 2};
+    const cuuint32_t obox[3] = {HD, OUT_ROWS, 1};
+    cr = enc(&tm_att, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, att, odims, ostrides, obox, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return GPT2_B200_EINVAL;
 
     Params p;
-    p.att = att;
-    p.att_seq_stride = att_seq_stride;
     p.T = T;
     p.H = H;
     p.E = E;
@@ -627,7 +663,7 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     // Persistent: at most CTAS_PER_SM resident CTAs per SM, each looping over its share of items.
     const long long slots = static_cast<long long>(CTAS_PER_SM) * (ctx->num_sms > 0 ? ctx->num_sms : 148);
     const unsigned grid = static_cast<unsigned>(total < slots ? total : slots);
-    k_flash_prefill_tc<<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, p);
+    k_flash_prefill_tc<<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, p);
     return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 

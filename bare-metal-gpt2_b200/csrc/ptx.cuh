@@ -106,6 +106,29 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// 3-D tiled TMA store shared -> global (this GPU's memory only), tracked by the issuing thread's
+// bulk async-group. Box rows outside the tensor map's extent are not written. The smem writes it
+// reads must be made visible to the async proxy first (fence_proxy_async_smem by each writer).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int c0, int c1,
+                                             int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores have finished READING shared memory (the source
+// may be overwritten); the global writes may still be in flight.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores are complete (global writes performed).
+__device__ __forceinline__ void bulk_wait_group0() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
 
 // ---------------------------------------------------------------- tcgen05: TMEM
 // Warp-collective. Writes the TMEM base address of ncols columns (power of two >= 32) to *dst.

@@ -501,8 +501,8 @@ def main(argv=None):
             dec = bench_decode(torch, lib, G, min(args.steps, 400), args.warmup, CTX, seed=500 + rank)
             dec["roofline"] = {"bound": "hbm", "achieved": dec["kv_gbs_per_launch"], "peak": peaks["hbm_gbs"],
                                "unit": "GB/s", "frac": dec["kv_gbs_per_launch"] / peaks["hbm_gbs"],
-                               "traffic": profile_traffic("decode_split_ctx1023_L12"),
-                               "kernel": "k_decode_split"}
+                               "traffic": profile_traffic("decode_stream_ctx1023_L12"),
+                               "kernel": "k_decode_stream"}
             sec["decode_ctx1023"] = dec
             for c in (128, 512):
                 d = bench_decode(torch, lib, G, min(args.steps, 200), args.warmup, c, seed=700 + rank)
