@@ -37,7 +37,6 @@ constexpr int OFF_K = 0;
 constexpr int OFF_V = OFF_K + NSTAGE * STAGE_BYTES;
 constexpr int OFF_RED = OFF_V + NSTAGE * STAGE_BYTES;           // [NCW][64] o + [NCW] m + [NCW] l
 constexpr int OFF_BAR = OFF_RED + (NCW * HD + 2 * NCW) * 4;
-constexpr int SMEM_BYTES = OFF_BAR + 128;
 constexpr int PART_STRIDE = HD + 2;
 
 struct __align__(8) Bars {
@@ -46,6 +45,9 @@ struct __align__(8) Bars {
     int abort;
     int is_last;
 };
+static_assert(OFF_BAR % 8 == 0, "mbarriers need 8-byte alignment");
+constexpr int SMEM_BYTES = OFF_BAR + static_cast<int>(sizeof(Bars));
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 
 struct Params {
     const __half *q;
