@@ -181,21 +181,41 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------- GPU legs
-class Timer:
-    """CUDA events on one stream: whole-region start/end plus one pair per launch."""
+SM_HZ_MAX = 1.965e9  # B200 clocks.max.sm; a hold of N seconds asks for N * SM_HZ_MAX cycles
 
-    def __init__(self, torch, n):
-        self.t = torch
-        self.start = torch.cuda.Event(enable_timing=True)
-        self.end = torch.cuda.Event(enable_timing=True)
-        self.a = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
-        self.b = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
-    def region_ms(self):
-        return self.start.elapsed_time(self.end)
+def host_seconds_per_step(torch, enqueue, n):
+    """Host time to enqueue one step (measured on warm-up steps, GPU drained before and after)."""
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(n):
+        enqueue(i)
+    dt = time.perf_counter() - t0
+    torch.cuda.synchronize()
+    return dt / max(1, n)
 
-    def launch_ms(self):
-        return [a.elapsed_time(b) for a, b in zip(self.a, self.b)]
+
+def timed_region(torch, stream, steps, enqueue, host_step_s):
+    """Device time of `steps` back-to-back steps: one CUDA event pair around the whole region, on the
+    launching stream. Before the start event the stream is held by torch.cuda._sleep (a busy loop of a
+    fixed number of clock cycles, outside the region) long enough for the host to enqueue every step,
+    so the region measures the GPU executing the steps back to back rather than the host submitting
+    them (an event pair around each short launch would itself add microseconds). Returns (ms,
+    host_kept_ahead)."""
+    hold_s = steps * host_step_s * 1.5 + 0.002
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(hold_s * SM_HZ_MAX))
+    start.record(stream)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        enqueue(i)
+    enq_s = time.perf_counter() - t0
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end), enq_s < hold_s
 
 
 def seeded_fp16(torch, shape, seed, device):
@@ -220,28 +240,16 @@ def bench_prefill(torch, lib, steps, warmup, world, seed_base, batch_layers=LAYE
         if rc != 0:
             raise RuntimeError(f"prefill launch failed: {lib.gpt2_b200_strerror(rc).decode()}")
 
-    for i in range(warmup):
-        launch(i)
-    torch.cuda.synchronize()
-    tm = Timer(torch, steps)
+    host_s = host_seconds_per_step(torch, launch, warmup)
     barrier(world)
-    torch.cuda.synchronize()
-    tm.start.record(stream)
-    for i in range(steps):
-        tm.a[i].record(stream)
-        launch(i)
-        tm.b[i].record(stream)
-    tm.end.record(stream)
-    torch.cuda.synchronize()
+    region, ahead = timed_region(torch, stream, steps, launch, host_s)
     barrier(world)
     st = lib.gpt2_b200_status(1)
     if st:
         raise RuntimeError(f"device status 0x{st:x} after prefill bench")
-    region = tm.region_ms()
-    per_launch = tm.launch_ms()
-    return {"region_ms": region, "launch_ms_mean": statistics.mean(per_launch),
-            "launch_ms_median": statistics.median(per_launch), "rotating_sets": rot,
-            "set_bytes": in_bytes + batch_layers * p * E * 2, "launches": steps}
+    return {"region_ms": region, "launch_ms_mean": region / steps, "rotating_sets": rot,
+            "set_bytes": in_bytes + batch_layers * p * E * 2, "launches": steps,
+            "host_kept_ahead": ahead}
 
 
 def bench_prefill_per_layer(torch, lib, steps, warmup, seed):
@@ -256,17 +264,11 @@ def bench_prefill_per_layer(torch, lib, steps, warmup, seed):
         for L in range(LAYERS):
             lib.gpt2_attention_b200_stream(att[i % rot][L].data_ptr(), qkv[i % rot][L].data_ptr(), P,
                                            E, H, D, sh)
-    for i in range(warmup):
-        step(i)
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for i in range(steps):
-        step(i)
-    e.record(stream)
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
-    return {"ms_per_step": ms, "tflops": prefill_flops(P) / (ms * 1e-3) / 1e12, "launches_per_step": LAYERS}
+    host_s = host_seconds_per_step(torch, step, warmup)
+    region, ahead = timed_region(torch, stream, steps, step, host_s)
+    ms = region / steps
+    return {"ms_per_step": ms, "tflops": prefill_flops(P) / (ms * 1e-3) / 1e12, "launches_per_step": LAYERS,
+            "host_kept_ahead": ahead}
 
 
 def bench_decode(torch, lib, G, steps, warmup, ctx, seed):
@@ -294,28 +296,18 @@ def bench_decode(torch, lib, G, steps, warmup, ctx, seed):
             graphs.append(g)
     torch.cuda.current_stream().wait_stream(side)
     stream = torch.cuda.current_stream()
-    for i in range(warmup):
+
+    def step(i):
         graphs[i % rot].replay()
-    torch.cuda.synchronize()
-    tm = Timer(torch, steps)
-    tm.start.record(stream)
-    for i in range(steps):
-        tm.a[i].record(stream)
-        graphs[i % rot].replay()
-        tm.b[i].record(stream)
-    tm.end.record(stream)
-    torch.cuda.synchronize()
+    host_s = host_seconds_per_step(torch, step, warmup)
+    region, ahead = timed_region(torch, stream, steps, step, host_s)
     st = lib.gpt2_b200_status(1)
     if st:
         raise RuntimeError(f"device status 0x{st:x} after decode bench")
-    per = tm.launch_ms()
-    region = tm.region_ms()
     nbytes = decode_bytes(ctx)
-    return {"ctx": ctx, "us_per_step": region / steps * 1e3,
-            "kv_gbs": nbytes / (region / steps * 1e-3) / 1e9,
-            "launch_us_mean": statistics.mean(per) * 1e3,
-            "kv_gbs_per_launch": nbytes / (statistics.mean(per) * 1e-3) / 1e9,
-            "bytes_per_step": nbytes, "rotating_caches": rot}
+    us = region / steps * 1e3
+    return {"ctx": ctx, "us_per_step": us, "kv_gbs": nbytes / (us * 1e-6) / 1e9,
+            "bytes_per_step": nbytes, "rotating_caches": rot, "host_kept_ahead": ahead}
 
 
 def bench_e2e_prefill(torch, lib, steps, warmup, seed):
@@ -485,7 +477,10 @@ def main(argv=None):
                                "one batched launch per step",
                    "global_batch": world, "seq_len": P, "layers": LAYERS, "parallelism": f"seq-shard x{world}",
                    "l2": f"{pre['rotating_sets']} rotating input sets of {pre['set_bytes'] / 1e6:.1f} MB "
-                         f"(> 126 MB L2 in total)"},
+                         f"(> 126 MB L2 in total)",
+                   "timing": "one CUDA event pair around the K back-to-back steps; the stream is held by a "
+                             "fixed-cycle busy kernel before the start event while the host queues them",
+                   "host_kept_ahead": pre["host_kept_ahead"]},
         "gpu_launches": pre["launches"],
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
@@ -499,14 +494,14 @@ def main(argv=None):
         sec = {}
         try:
             dec = bench_decode(torch, lib, G, min(args.steps, 400), args.warmup, CTX, seed=500 + rank)
-            dec["roofline"] = {"bound": "hbm", "achieved": dec["kv_gbs_per_launch"], "peak": peaks["hbm_gbs"],
-                               "unit": "GB/s", "frac": dec["kv_gbs_per_launch"] / peaks["hbm_gbs"],
+            dec["roofline"] = {"bound": "hbm", "achieved": dec["kv_gbs"], "peak": peaks["hbm_gbs"],
+                               "unit": "GB/s", "frac": dec["kv_gbs"] / peaks["hbm_gbs"],
                                "traffic": profile_traffic("decode_stream_ctx1023_L12"),
                                "kernel": "k_decode_stream"}
             sec["decode_ctx1023"] = dec
             for c in (128, 512):
                 d = bench_decode(torch, lib, G, min(args.steps, 200), args.warmup, c, seed=700 + rank)
-                sec[f"decode_ctx{c}"] = {k: d[k] for k in ("us_per_step", "kv_gbs", "launch_us_mean")}
+                sec[f"decode_ctx{c}"] = {k: d[k] for k in ("us_per_step", "kv_gbs", "host_kept_ahead")}
             sec["prefill_per_layer_launches"] = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
             sec["batched_B64"] = bench_batched(torch, lib, 3, args.warmup, world, rank, seed=1200 + rank)
             e2e = bench_e2e_prefill(torch, lib, min(args.steps, 30), args.warmup, seed=1300 + rank)
