@@ -8,12 +8,13 @@
 // built to keep every SM's share of HBM busy from start to finish:
 //   - grid = (split, head, job) sized to about one CTA per SM; for the 12-layer GPT-2 step that is
 //     one CTA per (layer, head) streaming its whole context, so no cross-CTA merge is needed at all;
-//   - warp 8 (one thread) issues cp.async.bulk copies of 64-key stages (8 KB of K + 8 KB of V, the
-//     slabs are contiguous) into a 4-stage shared-memory ring, tracked by mbarriers;
-//   - warps 0-7 each own 8 keys of every stage: 4 lanes per key (16 dims each, q held pre-scaled by
+//   - warp 16 (one thread) issues cp.async.bulk copies of 128-key stages (16 KB of K + 16 KB of V,
+//     the slabs are contiguous) into a 4-stage shared-memory ring, tracked by mbarriers (128 KB in
+//     flight per SM: with more, the copies only queue longer in the memory system);
+//   - warps 0-15 each own 8 keys of every stage: 4 lanes per key (16 dims each, q held pre-scaled by
 //     log2(e)/8 in registers), two xor-shuffles per score, a warp-level online softmax (running max,
 //     sum and 2 output dims per lane) with the hardware ex2, and V rows read as 128-byte lines;
-//   - the 8 warps' (m, l, o) are merged once in shared memory; only when a (job, head) is split over
+//   - the 16 warps' (m, l, o) are merged once in shared memory; only when a (job, head) is split over
 //     several CTAs (few jobs, e.g. one layer) do partials go through the workspace and the last CTA to
 //     arrive merges them (atomic counter, re-armed to zero for the next call / graph replay).
 // Every mbarrier wait is bounded; a timeout sets a status bit and the CTA unwinds after its own
@@ -27,12 +28,12 @@ namespace b200 {
 namespace dstream {
 
 constexpr int HD = 64;
-constexpr int NCW = 8;                       // consumer warps
+constexpr int NCW = 16;                      // consumer warps
 constexpr int NT = 32 * (NCW + 1);           // + one producer warp
-constexpr int KPS = 64;                      // keys per stage
+constexpr int KPS = 8 * NCW;                 // keys per stage: 8 per consumer warp
 constexpr int NSTAGE = 4;
 constexpr int ROW_BYTES = HD * 2;            // 128 B per key row
-constexpr int STAGE_BYTES = KPS * ROW_BYTES; // 8 KB of K (and 8 KB of V)
+constexpr int STAGE_BYTES = KPS * ROW_BYTES; // 16 KB of K (and 16 KB of V)
 constexpr int OFF_K = 0;
 constexpr int OFF_V = OFF_K + NSTAGE * STAGE_BYTES;
 constexpr int OFF_RED = OFF_V + NSTAGE * STAGE_BYTES;           // [NCW][64] o + [NCW] m + [NCW] l
