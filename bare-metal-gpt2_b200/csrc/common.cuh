@@ -33,6 +33,10 @@ struct DeviceContext {
     unsigned *counters = nullptr;   // decode split-arrival counters (kept at zero between calls)
     size_t part_floats = 0;
     size_t counter_words = 0;
+    float *pf_part = nullptr;       // prefill: partial rows of split work units
+    unsigned *pf_counters = nullptr;  // prefill: chunk arrivals per 32 rows (kept at zero)
+    size_t pf_part_floats = 0;
+    size_t pf_counter_words = 0;
     bool prefill_attr_done = false;
     bool decode_attr_done = false;
     int num_sms = 0;

@@ -35,6 +35,7 @@
 // TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 224.5 KB
 // (Q 64 KB, K and V rings 128 KB, output slots 32 KB, barriers). No cluster, no multicast. Every
 // mbarrier wait is bounded.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 
@@ -98,40 +99,73 @@ struct Params {
     int T, H, E, B;
     int n_qtiles;
     int n_pairs;               // ceil(n_qtiles / 2)
-    int total_items;           // n_pairs * H * B
+    int kv_chunk;              // K/V tiles per work unit (>= n_qtiles: a pair is never split)
+    int units_per_hb;          // work units per (head, sequence): sum over pairs of their chunks
+    int max_chunks;            // chunks of the longest pair (partial-row slots per query tile)
+    int total_items;           // units_per_hb * H * B
     float scale_log2;          // log2(e) / sqrt(D)
+    float *part;               // split units: partials [group][chunk][PART_COLS][128 rows]
+    unsigned *counters;        // split units: arrivals per [group][lane quarter], re-armed to 0
     unsigned *status;
     unsigned long long timeout_ns;
 };
+constexpr int PART_COLS = HD + 2;  // o[64], m, l of a row; stored column-major (coalesced)
+constexpr int MAX_CHUNKS = 8;       // chunks per pair at most (the merge is unrolled over them)
 
 struct Item {
     int pair, h, b;
-    int nk[2];  // K/V tiles of query tile A (2p+1) and of B (2p+2, or 0 when tile 2p+1 is past T)
-    int nkv;    // K/V tiles loaded for the item: max(nk)
+    int kv0;             // first K/V tile of this unit (its chunk of the pair's key range)
+    int chunk, nchunk;   // chunk index and chunks of this pair (nchunk > 1: partial rows + merge)
+    int nk[2];  // K/V tiles of query tile A (2p) and of B (2p+1, none past T) in this unit: a prefix
+    int nkv;    // K/V tiles loaded for the unit: max(nk)
     // nk[x] for a runtime x without a local-memory array access
     __device__ __forceinline__ int nk_of(int x) const { return x ? nk[1] : nk[0]; }
 };
 
-// The r-th item of this CTA. Items are numbered heaviest first (the last pair of every head and
-// sequence first); rounds alternate direction (snake) so that each CTA gets a mix of heavy and light
-// pairs. Returns false when this CTA has no r-th item (nor any later one).
+// K/V tiles a pair's key range covers: through B's diagonal, or A's when B is past T.
+__device__ __forceinline__ int pair_kv_tiles(const Params &p, int pair) {
+    return (2 * pair + 1 < p.n_qtiles) ? 2 * pair + 2 : 2 * pair + 1;
+}
+
+// The r-th work unit of this CTA. A unit is one chunk of kv_chunk K/V tiles of a pair of query tiles
+// (the whole key range unless the launch is too small to fill the SMs with whole pairs). Units are
+// numbered heaviest pair first; rounds alternate direction (snake) so that each CTA gets a mix of
+// heavy and light units. Returns false when this CTA has no r-th unit (nor any later one).
+template <bool kSplit>
 __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
     const int G = gridDim.x, c = blockIdx.x;
     const long long i = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - c) : c);
     if (i >= p.total_items) return false;
     const int per = p.H * p.B;
     const int idx = static_cast<int>(i);
-    it.pair = p.n_pairs - 1 - idx / per;
+    int u = idx / per;  // unit within its (head, sequence)
     const int rem = idx % per;
     it.h = rem % p.H;
     it.b = rem / p.H;
-    it.nk[0] = 2 * it.pair + 1;
-    it.nk[1] = (2 * it.pair + 1 < p.n_qtiles) ? 2 * it.pair + 2 : 0;
-    it.nkv = it.nk[1] ? it.nk[1] : it.nk[0];
+    int pr = p.n_pairs - 1 - u, nc = 1;  // whole pairs: unit u is pair n_pairs-1-u, one chunk
+    if (kSplit) {
+        for (pr = p.n_pairs - 1; pr > 0; --pr) {
+            nc = (pair_kv_tiles(p, pr) + p.kv_chunk - 1) / p.kv_chunk;
+            if (u < nc) break;
+            u -= nc;
+        }
+        if (pr == 0) nc = (pair_kv_tiles(p, 0) + p.kv_chunk - 1) / p.kv_chunk;
+    } else {
+        u = 0;
+    }
+    it.pair = pr;
+    it.chunk = u;
+    it.nchunk = nc;
+    it.kv0 = u * p.kv_chunk;
+    const int hi = min(it.kv0 + p.kv_chunk, pair_kv_tiles(p, pr));
+    it.nk[0] = max(0, min(hi, 2 * pr + 1) - it.kv0);
+    it.nk[1] = (2 * pr + 1 < p.n_qtiles) ? hi - it.kv0 : 0;
+    it.nkv = hi - it.kv0;
     return true;
 }
 
 // A cursor over this CTA's K/V tiles in processing order (item by item).
+template <bool kSplit>
 struct Cursor {
     Item I;
     int it, j, g;  // item number, K/V tile within the item, K/V tile number over all items
@@ -140,14 +174,14 @@ struct Cursor {
         it = 0;
         j = 0;
         g = 0;
-        valid = get_item(p, 0, I);
+        valid = get_item<kSplit>(p, 0, I);
     }
     __device__ __forceinline__ void advance(const Params &p) {
         ++g;
         if (++j == I.nkv) {
             j = 0;
             ++it;
-            valid = get_item(p, it, I);
+            valid = get_item<kSplit>(p, it, I);
         }
     }
 };
@@ -165,12 +199,13 @@ __device__ __forceinline__ bool aborted(Bars *bars) {
 // Load order: the Q tiles of an item before its first K; then K(t), V(t-1), K(t+1), V(t), ... . K
 // stages are released when their QKs complete and V stages when their PVs complete (later), so
 // issuing V one tile behind K keeps the K loads from queueing behind a V wait.
+template <bool kSplit>
 __device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, const Params &p) {
     const unsigned long long to = p.timeout_ns;
     int last_q[NQ] = {-1, -1}, last_k[NSTAGE], last_v[NSTAGE];
     for (int s = 0; s < NSTAGE; ++s) last_k[s] = last_v[s] = -1;
     bool ok = true;
-    Cursor kc, vc;  // next K tile to load; next V tile to load (never ahead of kc)
+    Cursor<kSplit> kc, vc;  // next K tile to load; next V tile to load (never ahead of kc)
     kc.start(p);
     vc.start(p);
     auto load_v = [&]() -> bool {
@@ -178,7 +213,7 @@ __device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, c
         if (vc.g >= NSTAGE && !mbar_wait(&bars->v_empty[s], ((vc.g / NSTAGE) - 1) & 1, to)) return false;
         mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
         tma_load_3d(smem + OFF_V + s * TILE_BYTES, tm, &bars->v_full[s], 2 * p.E + vc.I.h * HD,
-                    vc.j * BN, vc.I.b);
+                    (vc.I.kv0 + vc.j) * BN, vc.I.b);
         last_v[s] = vc.g;
         vc.advance(p);
         return true;
@@ -203,7 +238,7 @@ __device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, c
             break;
         mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
         tma_load_3d(smem + OFF_K + s * TILE_BYTES, tm, &bars->k_full[s], p.E + kc.I.h * HD,
-                    kc.j * BN, kc.I.b);
+                    (kc.I.kv0 + kc.j) * BN, kc.I.b);
         last_k[s] = kc.g;
         kc.advance(p);
         if (vc.g + 1 < kc.g && !(ok = load_v())) break;  // V one tile behind K
@@ -226,6 +261,7 @@ __device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, c
 // dependencies. Both walk every K/V tile of every item; the shared K, V and Q stages are released
 // through two-arrival barriers: a stream commits its MMAs on them (or, for a tile it does not use,
 // arrives after that tile has landed, so that arrivals of different phases cannot mix).
+template <bool kSplit>
 __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int x) {
     const unsigned long long to = p.timeout_ns;
     Stream &S = bars->st[x];
@@ -245,7 +281,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
     int gp = 0;   // this query tile's PVs issued
     int itp = 0;  // items in which this query tile's PVs have started (for o_free)
     // S = Q K^T for the K/V tile under cursor q (or release of that tile if this query tile skips it).
-    auto qk_step = [&](const Cursor &q) -> bool {
+    auto qk_step = [&](const Cursor<kSplit> &q) -> bool {
         const int qb = q.it % NQ, s = q.g % NSTAGE;
         const bool uses = q.j < q.I.nk_of(x);
         if (q.j == 0 && !mbar_wait(&bars->q_full[qb], (q.it / NQ) & 1, to)) return false;
@@ -272,7 +308,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
         return true;
     };
     // O += P V for the K/V tile under cursor v (or release of that tile).
-    auto pv_step = [&](const Cursor &v) -> bool {
+    auto pv_step = [&](const Cursor<kSplit> &v) -> bool {
         const int s = v.g % NSTAGE;
         if (!mbar_wait(&bars->v_full[s], (v.g / NSTAGE) & 1, to)) return false;
         if (v.j >= v.I.nk_of(x)) {
@@ -296,7 +332,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
         return true;
     };
 
-    Cursor q, v;  // q: next K/V tile for QK; v: next tile for PV (one behind q)
+    Cursor<kSplit> q, v;  // q: next K/V tile for QK; v: next tile for PV (one behind q)
     q.start(p);
     v.start(p);
     bool ok = true;
@@ -329,6 +365,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
 
 // Softmax of query tile x (0 = A, 1 = B) of every item: 4 warps, thread = one query row (TMEM lane),
 // all 128 scores of a tile in registers.
+template <bool kSplit>
 __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CUtensorMap *tm_att,
                             uint32_t tbase, int x, int warp, int lane) {
     const unsigned long long to = p.timeout_ns;
@@ -354,9 +391,11 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
     int ex2_phases = 0;  // this warp's completed ex2 phases
     bool ok = true;
     Item I;
-    for (int it = 0; ok && get_item(p, it, I); ocum += I.nk_of(x ^ 1), ++it) {
+    for (int it = 0; ok && get_item<kSplit>(p, it, I); ocum += I.nk_of(x ^ 1), ++it) {
         const int nk = I.nk_of(x);
-        if (nk == 0) continue;     // no tile B in this item
+        if (nk == 0) continue;     // this query tile has no keys in this unit
+        const int nk_other = I.nk_of(x ^ 1);
+        const int diag_j = 2 * I.pair + x - I.kv0;  // unit tile holding this tile's diagonal
         float m_used = -INFINITY;  // running max (log2 units) used for the exponentials
         float l = 0.f;             // running sum of the (fp16-rounded) exponentials
         for (int j = 0; j < nk; ++j, ++g) {
@@ -378,7 +417,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.s_free);  // the next QK may overwrite S
 
-            if (j == nk - 1) {  // diagonal tile (BM == BN): key k is visible iff k <= r
+            if (j == diag_j) {  // diagonal tile (BM == BN): key k is visible iff k <= r
                 const int r = quarter * 32 + lane;
 #pragma unroll
                 for (int i = 0; i < BN; ++i)
@@ -409,7 +448,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
                 tc_fence_after();
             }
             {  // wait for our turn on this sub-partition's MUFU (time-bounded spin on the counter)
-                const int need = ocum + min(j + x, I.nk_of(x ^ 1));
+                const int need = ocum + min(j + x, nk_other);
                 int ready = 1;
                 if (lane == 0 && need > 0) {
                     const volatile int *cnt = &O.ex2_done[quarter];
@@ -472,20 +511,31 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
             if (lane == 0) mbar_arrive(&S.p_full);
         }
         if (!ok) break;
-        // ---- epilogue of this item: O / l -> fp16 -> this warp's output slot -> one TMA store of
-        // its 32 rows (rows past T are clipped by the tensor map)
+        // ---- epilogue of this unit: O / l -> fp16 -> this warp's output slot -> one TMA store of
+        // its 32 rows (rows past T are clipped by the tensor map). A split unit first parks its
+        // unnormalised rows in the workspace; the last chunk to arrive merges them.
         ok = warp_wait(&S.o_done, (g - 1) & 1, to);
         if (!ok) break;
         tc_fence_after();
+        get_item<kSplit>(p, it, I);  // re-derived rather than kept live through the tile loop
         // the slot's previous store has finished reading it (returns at once if none is pending)
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
-        {
+        // This warp's output slot: its 32 rows x 64 columns, row `lane` at lane * 128 B, 16-byte
+        // chunk k of a row at chunk position k ^ (row % 8) (the TMA 128-byte swizzle, which also
+        // makes these writes bank-conflict-free).
+        uint8_t *my_row = smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT + lane * (HD * 2);
+        auto put32 = [&](int cb, const uint32_t(&o)[16]) {  // 32 fp16 columns of this row
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int chunk = (4 * cb + q) ^ (lane & 7);
+                *reinterpret_cast<uint4 *>(my_row + chunk * 16) =
+                    make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            }
+        };
+        bool store = true;  // this warp holds the final rows of its 32 queries
+        if (!kSplit || I.nchunk == 1) {
             const float inv_l = 1.f / l;
-            // This warp's output slot: its 32 rows x 64 columns, row `lane` at lane * 128 B, 16-byte
-            // chunk k of a row at chunk position k ^ (row % 8) (the TMA 128-byte swizzle, which also
-            // makes these writes bank-conflict-free).
-            uint8_t *my_row = smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT + lane * (HD * 2);
 #pragma unroll
             for (int cb = 0; cb < 2; ++cb) {  // 32 columns of O at a time
                 uint32_t v[32];
@@ -496,22 +546,83 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
                 for (int i = 0; i < 16; ++i)
                     o[i] = pack_half2(__uint_as_float(v[2 * i]) * inv_l,
                                       __uint_as_float(v[2 * i + 1]) * inv_l);
+                put32(cb, o);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
+        } else {
+            const long long grp =
+                ((static_cast<long long>(I.b) * p.H + I.h) * p.n_pairs + I.pair) * 2 + x;
+            const int row = quarter * OUT_ROWS + lane;
+            // column c of this row of chunk k at part[((grp * max_chunks + k) * PART_COLS + c) * 128 + row]
+            float *mine = p.part + (grp * p.max_chunks + I.chunk) * (PART_COLS * BM) + row;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int chunk = (4 * cb + q) ^ (lane & 7);
-                    *reinterpret_cast<uint4 *>(my_row + chunk * 16) =
-                        make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            for (int cb = 0; cb < 2; ++cb) {
+                uint32_t v[32];
+                tmem_ld32(tO + 32 * cb, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mine[(32 * cb + i) * BM] = __uint_as_float(v[i]);
+            }
+            mine[HD * BM] = m_used;
+            mine[(HD + 1) * BM] = l;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.o_free);
+            __threadfence();  // this row's partial is visible device-wide before the arrival
+            __syncwarp();
+            unsigned *cnt = p.counters + grp * 4 + quarter;
+            const int ncx = (2 * I.pair + x + p.kv_chunk) / p.kv_chunk;  // chunks with this tile's keys
+            unsigned prev = 0;
+            if (lane == 0) prev = atomicAdd(cnt, 1u);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            store = (prev == static_cast<unsigned>(ncx - 1));
+            if (store) {  // last chunk of these 32 rows: merge every chunk's partial row
+                __threadfence();
+                const float *base = p.part + grp * p.max_chunks * (PART_COLS * BM) + row;
+                float mk[MAX_CHUNKS], w[MAX_CHUNKS];
+                float M = -INFINITY;
+#pragma unroll
+                for (int k = 0; k < MAX_CHUNKS; ++k) {
+                    mk[k] = k < ncx ? __ldcg(base + k * (PART_COLS * BM) + HD * BM) : -INFINITY;
+                    M = fmaxf(M, mk[k]);
                 }
+                float L = 0.f;
+#pragma unroll
+                for (int k = 0; k < MAX_CHUNKS; ++k) {
+                    w[k] = k < ncx ? ex2_approx(mk[k] - M) : 0.f;
+                    if (k < ncx) L = fmaf(w[k], __ldcg(base + k * (PART_COLS * BM) + (HD + 1) * BM), L);
+                }
+                const float inv_l = 1.f / L;
+#pragma unroll
+                for (int cb = 0; cb < 2; ++cb) {
+                    float acc[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll
+                    for (int k = 0; k < MAX_CHUNKS; ++k)
+                        if (k < ncx) {
+                            const float *pc = base + k * (PART_COLS * BM) + (32 * cb) * BM;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) acc[i] = fmaf(w[k], __ldcg(pc + i * BM), acc[i]);
+                        }
+                    uint32_t o[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = pack_half2(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
+                    put32(cb, o);
+                }
+                if (lane == 0) *cnt = 0u;  // re-armed for the next launch (every chunk has arrived)
             }
         }
-        tc_fence_before();
-        fence_proxy_async_smem();  // this thread's slot writes -> visible to the TMA engine
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
-        const int row0 = (2 * I.pair + x) * BM + quarter * OUT_ROWS;
-        if (lane == 0 && row0 < p.T) {  // rows past T inside the box are clipped by the tensor map
-            tma_store_3d(tm_att, smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT, I.h * HD, row0, I.b);
-            bulk_commit_group();
+        if (store) {
+            fence_proxy_async_smem();  // this thread's slot writes -> visible to the TMA engine
+            __syncwarp();
+            const int row0 = (2 * I.pair + x) * BM + quarter * OUT_ROWS;
+            if (lane == 0 && row0 < p.T) {  // rows past T inside the box are clipped by the tensor map
+                tma_store_3d(tm_att, smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT, I.h * HD, row0, I.b);
+                bulk_commit_group();
+            }
         }
     }
     if (!ok) raise_abort(bars, p.status, ST_PREFILL_SOFTMAX_TIMEOUT);
@@ -521,6 +632,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
     __syncwarp();
 }
 
+template <bool kSplit>
 __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv,
                        const __grid_constant__ CUtensorMap tm_att, const Params p) {
@@ -567,13 +679,13 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     const uint32_t tbase = bars->tmem_base;
 
     if (warp == 0) {
-        if (lane == 0) run_producer(&tm_qkv, smem, bars, p);
+        if (lane == 0) run_producer<kSplit>(&tm_qkv, smem, bars, p);
         __syncwarp();
     } else if (warp == 1 || warp == MMA_B_WARP) {
-        if (lane == 0) run_mma(smem, bars, p, tbase, warp == 1 ? 0 : 1);
+        if (lane == 0) run_mma<kSplit>(smem, bars, p, tbase, warp == 1 ? 0 : 1);
         __syncwarp();
     } else {
-        run_softmax(smem, bars, p, &tm_att, tbase, (warp - 2) / NSOFT_WARPS, warp, lane);
+        run_softmax<kSplit>(smem, bars, p, &tm_att, tbase, (warp - 2) / NSOFT_WARPS, warp, lane);
     }
 
     tc_fence_before();
@@ -605,7 +717,62 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// Chunk size (K/V tiles per work unit) for a launch of n_pairs pairs per (head, sequence) on `sms`
+// SMs. Time model in units of one K/V tile step of a pair (both query tiles): a CTA's share of the
+// total work, or the longest single unit, whichever is larger. A unit costs its tiles plus a fixed
+// part measured on B200: ~2.2 steps for a whole pair (first loads, epilogue) and ~7 steps for a
+// split one (the partial rows' write-out, fences and the merge are a chain of memory round trips).
+// Large launches keep whole pairs; small ones (one layer of one sequence at P >= 1024) split the
+// long key ranges when that clearly shortens the longest unit.
+static int choose_kv_chunk(int n_qtiles, int n_pairs, long long hb, int sms) {
+    int best = n_qtiles;
+    double best_t = 1e300;
+    const int cs_min = std::max(2, (n_qtiles + MAX_CHUNKS - 1) / MAX_CHUNKS);
+    for (int cs = n_qtiles; cs >= cs_min; --cs) {
+        long long units = 0, tiles = 0;
+        for (int pr = 0; pr < n_pairs; ++pr) {
+            const int nkv = (2 * pr + 1 < n_qtiles) ? 2 * pr + 2 : 2 * pr + 1;
+            units += (nkv + cs - 1) / cs;
+            tiles += nkv;
+        }
+        const bool split = units > n_pairs;
+        const double ov = split ? 7.0 : 2.2;
+        const double share = (static_cast<double>(tiles) * hb + units * hb * ov) / sms;
+        const double longest = std::min(cs, n_qtiles) + ov;
+        const double t = std::max(share, longest);
+        if (t < best_t * 0.97) {  // prefer fewer, larger units unless splitting clearly pays
+            best_t = t;
+            best = cs;
+        }
+    }
+    return best;
+}
+
 }  // namespace prefill
+
+// Partial-row workspace of split prefill units (grown on demand, never while capturing).
+static bool ensure_prefill_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream) {
+    if (ctx->pf_part_floats >= floats && ctx->pf_counter_words >= words) return true;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+    if (cudaDeviceSynchronize() != cudaSuccess) return false;
+    if (ctx->pf_part_floats < floats) {
+        if (ctx->pf_part) cudaFree(ctx->pf_part);
+        ctx->pf_part = nullptr;
+        ctx->pf_part_floats = 0;
+        if (cudaMalloc(&ctx->pf_part, floats * sizeof(float)) != cudaSuccess) return false;
+        ctx->pf_part_floats = floats;
+    }
+    if (ctx->pf_counter_words < words) {
+        if (ctx->pf_counters) cudaFree(ctx->pf_counters);
+        ctx->pf_counters = nullptr;
+        ctx->pf_counter_words = 0;
+        if (cudaMalloc(&ctx->pf_counters, words * sizeof(unsigned)) != cudaSuccess) return false;
+        if (cudaMemset(ctx->pf_counters, 0, words * sizeof(unsigned)) != cudaSuccess) return false;
+        ctx->pf_counter_words = words;
+    }
+    return true;
+}
 
 // Launches the batched causal prefill. Arguments are validated by the caller (api.cu).
 int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
@@ -616,11 +783,13 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     EncodeTiledFn enc = encode_fn();
     if (!enc) return GPT2_B200_EDEVICE;
     if (!ctx->prefill_attr_done) {
-        if (cudaFuncSetAttribute(k_flash_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 SMEM_BYTES) != cudaSuccess)
-            return GPT2_B200_ECUDA;
-        cudaFuncSetAttribute(k_flash_prefill_tc, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
+        for (auto fn : {k_flash_prefill_tc<false>, k_flash_prefill_tc<true>}) {
+            if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess)
+                return GPT2_B200_ECUDA;
+            cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
+        }
         ctx->prefill_attr_done = true;
     }
     CUtensorMap tm;
@@ -653,7 +822,30 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     p.B = B;
     p.n_qtiles = (T + BM - 1) / BM;
     p.n_pairs = (p.n_qtiles + 1) / 2;
-    const long long total = static_cast<long long>(p.n_pairs) * H * B;
+    const long long hb = static_cast<long long>(H) * B;
+    const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+    p.kv_chunk = p.n_qtiles;  // whole pairs
+    p.units_per_hb = p.n_pairs;
+    p.max_chunks = 1;
+    p.part = nullptr;
+    p.counters = nullptr;
+    if (hb * p.n_pairs < sms) {
+        const int cs = choose_kv_chunk(p.n_qtiles, p.n_pairs, hb, sms);
+        int units = 0;
+        for (int pr = 0; pr < p.n_pairs; ++pr)
+            units += (((2 * pr + 1 < p.n_qtiles) ? 2 * pr + 2 : 2 * pr + 1) + cs - 1) / cs;
+        const int max_chunks = (p.n_qtiles + cs - 1) / cs;
+        const size_t groups = static_cast<size_t>(hb) * p.n_pairs * 2;
+        if (units > p.n_pairs &&
+            ensure_prefill_workspace(ctx, groups * max_chunks * BM * PART_COLS, groups * 4, stream)) {
+            p.kv_chunk = cs;
+            p.units_per_hb = units;
+            p.max_chunks = max_chunks;
+            p.part = ctx->pf_part;
+            p.counters = ctx->pf_counters;
+        }
+    }
+    const long long total = static_cast<long long>(p.units_per_hb) * hb;
     if (total <= 0) return GPT2_B200_OK;
     if (total > 0x7fffffffLL) return GPT2_B200_EINVAL;
     p.total_items = static_cast<int>(total);
@@ -663,7 +855,10 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     // Persistent: at most CTAS_PER_SM resident CTAs per SM, each looping over its share of items.
     const long long slots = static_cast<long long>(CTAS_PER_SM) * (ctx->num_sms > 0 ? ctx->num_sms : 148);
     const unsigned grid = static_cast<unsigned>(total < slots ? total : slots);
-    k_flash_prefill_tc<<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, p);
+    if (p.units_per_hb != p.n_pairs)
+        k_flash_prefill_tc<true><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, p);
+    else
+        k_flash_prefill_tc<false><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, p);
     return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 
