@@ -42,8 +42,11 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 DeviceContext *device_context() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    // A context never changes once created, so each host thread keeps its pointer (no lock).
+    thread_local DeviceContext *t_ctx[kMaxDevices] = {};
+    if (t_ctx[dev]) return t_ctx[dev];
     std::lock_guard<std::mutex> lk(g_mu);
-    if (g_ctx_ready[dev]) return &g_ctx[dev];
+    if (g_ctx_ready[dev]) return t_ctx[dev] = &g_ctx[dev];
     if (g_ctx_err[dev]) return nullptr;
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10) {
@@ -52,6 +55,7 @@ DeviceContext *device_context() {
     }
     DeviceContext &c = g_ctx[dev];
     c.num_sms = prop.multiProcessorCount;
+    c.device = dev;
     if (cudaMalloc(&c.status, sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(c.status, 0, sizeof(unsigned)) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
@@ -59,7 +63,7 @@ DeviceContext *device_context() {
         return nullptr;
     }
     g_ctx_ready[dev] = true;
-    return &c;
+    return t_ctx[dev] = &c;
 }
 
 unsigned long long wait_timeout_ns() {

@@ -40,6 +40,7 @@ struct DeviceContext {
     bool prefill_attr_done = false;
     bool decode_attr_done = false;
     int num_sms = 0;
+    int device = 0;                 // CUDA device ordinal of this context
 };
 
 // Returns the context of the current device (creating it on first use), or nullptr on CUDA error.

@@ -517,7 +517,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
         ok = warp_wait(&S.o_done, (g - 1) & 1, to);
         if (!ok) break;
         tc_fence_after();
-        get_item<kSplit>(p, it, I);  // re-derived rather than kept live through the tile loop
+        if (kSplit) get_item<kSplit>(p, it, I);  // re-derived, not kept live through the tile loop
         // the slot's previous store has finished reading it (returns at once if none is pending)
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
@@ -750,6 +750,38 @@ static int choose_kv_chunk(int n_qtiles, int n_pairs, long long hb, int sms) {
 
 }  // namespace prefill
 
+// Per-thread cache of recently encoded tensor maps (kind 0 = qkv load map, 1 = att store map).
+namespace {
+struct MapEntry {
+    int kind, device, E, T, B;
+    const void *ptr;
+    long long seq_stride;
+    bool valid;
+    CUtensorMap map;
+};
+constexpr int kMapCache = 8;
+thread_local MapEntry t_maps[kMapCache];
+thread_local int t_map_next = 0;
+}  // namespace
+
+static bool cached_map(int kind, const void *ptr, int E, int T, int B, long long seq_stride, int device,
+                       CUtensorMap *out) {
+    for (const MapEntry &e : t_maps)
+        if (e.valid && e.kind == kind && e.ptr == ptr && e.E == E && e.T == T && e.B == B &&
+            e.seq_stride == seq_stride && e.device == device) {
+            *out = e.map;
+            return true;
+        }
+    return false;
+}
+
+static void remember_map(int kind, const void *ptr, int E, int T, int B, long long seq_stride, int device,
+                         const CUtensorMap &map) {
+    MapEntry &e = t_maps[t_map_next];
+    t_map_next = (t_map_next + 1) % kMapCache;
+    e = MapEntry{kind, device, E, T, B, ptr, seq_stride, true, map};
+}
+
 // Partial-row workspace of split prefill units (grown on demand, never while capturing).
 static bool ensure_prefill_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream) {
     if (ctx->pf_part_floats >= floats && ctx->pf_counter_words >= words) return true;
@@ -792,28 +824,36 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
         }
         ctx->prefill_attr_done = true;
     }
-    CUtensorMap tm;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(3 * E), static_cast<cuuint64_t>(T),
-                                static_cast<cuuint64_t>(B)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(3 * E) * 2,
-                                   static_cast<cuuint64_t>(qkv_seq_stride) * 2};
-    const cuuint32_t box[3] = {HD, BM, 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult cr = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(qkv), dims,
-                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return GPT2_B200_EINVAL;
-    // att [B][T][E] (sequence stride att_seq_stride): one store box = 32 rows x 64 columns of a head
-    CUtensorMap tm_att;
-    const cuuint64_t odims[3] = {static_cast<cuuint64_t>(E), static_cast<cuuint64_t>(T),
-                                 static_cast<cuuint64_t>(B)};
-    const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(E) * 2,
-                                    static_cast<cuuint64_t>(att_seq_stride) * 2};
-    const cuuint32_t obox[3] = {HD, OUT_ROWS, 1};
-    cr = enc(&tm_att, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, att, odims, ostrides, obox, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return GPT2_B200_EINVAL;
+    // qkv [B][T][3E] read as 64 x 128 boxes; att [B][T][E] written as 64 x 32 boxes (one per softmax
+    // warp). Encoding is host work (microseconds), so the maps of recent calls are kept per thread:
+    // the reference's forward pass calls attention on the same buffers for every layer.
+    CUtensorMap tm, tm_att;
+    if (!cached_map(0, qkv, E, T, B, qkv_seq_stride, ctx->device, &tm)) {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(3 * E), static_cast<cuuint64_t>(T),
+                                    static_cast<cuuint64_t>(B)};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(3 * E) * 2,
+                                       static_cast<cuuint64_t>(qkv_seq_stride) * 2};
+        const cuuint32_t box[3] = {HD, BM, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(qkv), dims, strides, box,
+                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return GPT2_B200_EINVAL;
+        remember_map(0, qkv, E, T, B, qkv_seq_stride, ctx->device, tm);
+    }
+    if (!cached_map(1, att, E, T, B, att_seq_stride, ctx->device, &tm_att)) {
+        const cuuint64_t odims[3] = {static_cast<cuuint64_t>(E), static_cast<cuuint64_t>(T),
+                                     static_cast<cuuint64_t>(B)};
+        const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(E) * 2,
+                                        static_cast<cuuint64_t>(att_seq_stride) * 2};
+        const cuuint32_t obox[3] = {HD, OUT_ROWS, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (enc(&tm_att, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, att, odims, ostrides, obox, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return GPT2_B200_EINVAL;
+        remember_map(1, att, E, T, B, att_seq_stride, ctx->device, tm_att);
+    }
 
     Params p;
     p.T = T;
