@@ -310,31 +310,41 @@ def bench_decode(torch, lib, G, steps, warmup, ctx, seed):
             "bytes_per_step": nbytes, "rotating_caches": rot, "host_kept_ahead": ahead}
 
 
-def bench_e2e_prefill(torch, lib, steps, warmup, seed):
-    """End to end through the C ABI: pinned host qkv -> device, one launch, att -> pinned host."""
-    stream = torch.cuda.current_stream()
-    sh = stream.cuda_stream
+def bench_e2e_prefill(torch, lib, steps, warmup, seed, nstreams=3):
+    """End to end through the reference-facing C ABI with host buffers: per layer, pinned host qkv ->
+    device (cudaMemcpyAsync), gpt2_attention_b200_stream (the reference's GPT2Backend.attention slot,
+    with a stream), att -> pinned host. Layers rotate over `nstreams` streams, each with its own
+    one-layer device buffers, so one layer's upload, another's attention and a third's download
+    overlap. The step ends when every layer's output is back in host memory."""
+    main = torch.cuda.current_stream()
+    streams = [torch.cuda.Stream() for _ in range(nstreams)]
     host_in = [seeded_fp16(torch, (LAYERS, P, QKV), seed + i, "cpu").pin_memory() for i in range(2)]
     host_out = torch.empty((LAYERS, P, E), dtype=torch.float16).pin_memory()
-    d_in = torch.empty((LAYERS, P, QKV), dtype=torch.float16, device="cuda")
-    d_out = torch.empty((LAYERS, P, E), dtype=torch.float16, device="cuda")
+    d_in = [torch.empty((P, QKV), dtype=torch.float16, device="cuda") for _ in range(nstreams)]
+    d_out = [torch.empty((P, E), dtype=torch.float16, device="cuda") for _ in range(nstreams)]
+    start_ev = torch.cuda.Event()
 
     def step(i):
-        d_in.copy_(host_in[i % 2], non_blocking=True)
-        lib.gpt2_attention_b200_batched(d_out.data_ptr(), d_in.data_ptr(), LAYERS, P, E, H, D, 0, 0, sh)
-        host_out.copy_(d_out, non_blocking=True)
+        start_ev.record(main)
+        for L in range(LAYERS):
+            k = L % nstreams
+            st = streams[k]
+            st.wait_event(start_ev)
+            with torch.cuda.stream(st):
+                d_in[k].copy_(host_in[i % 2][L], non_blocking=True)
+                rc = lib.gpt2_attention_b200_stream(d_out[k].data_ptr(), d_in[k].data_ptr(), P, E, H, D,
+                                                    st.cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(f"e2e attention failed: {lib.gpt2_b200_strerror(rc).decode()}")
+                host_out[L].copy_(d_out[k], non_blocking=True)
+        for st in streams:
+            main.wait_stream(st)
 
-    for i in range(warmup):
-        step(i)
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for i in range(steps):
-        step(i)
-    e.record(stream)
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
-    return {"ms_per_step": ms, "h2d": LAYERS * P * QKV * 2, "d2h": LAYERS * P * E * 2}
+    host_s = host_seconds_per_step(torch, step, max(2, warmup))
+    region, ahead = timed_region(torch, main, steps, step, host_s)
+    ms = region / steps
+    return {"ms_per_step": ms, "h2d": LAYERS * P * QKV * 2, "d2h": LAYERS * P * E * 2,
+            "host_kept_ahead": ahead, "streams": nstreams}
 
 
 def bench_batched(torch, lib, steps, warmup, world, rank, seed):
@@ -508,8 +518,10 @@ def main(argv=None):
             e2e_ms = max_over_ranks(e2e["ms_per_step"], world)
             line["e2e"] = {"value": world * flops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                            "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                           "ms_per_step": e2e_ms,
-                           "path": "pinned host qkv -> cudaMemcpyAsync -> gpt2_attention_b200_batched -> att to pinned host"}
+                           "ms_per_step": e2e_ms, "host_kept_ahead": e2e["host_kept_ahead"],
+                           "path": "per layer: pinned host qkv -> cudaMemcpyAsync -> gpt2_attention_b200_stream "
+                                   f"(the reference's attention slot) -> att to pinned host, {e2e['streams']} "
+                                   "streams overlapping upload, attention and download"}
         except Exception as ex:  # noqa: BLE001 - the headline stands; the failure is reported
             sec["error"] = repr(ex)
         line["secondary"] = sec
