@@ -15,7 +15,8 @@
 namespace b200 {
 
 int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
-                   long long qkv_seq_stride, long long att_seq_stride, cudaStream_t stream);
+                   long long qkv_seq_stride, long long att_seq_stride, __half *kv_layer, int kv_maxT,
+                   cudaStream_t stream);
 int launch_decode(__half *out, long long out_stride, const __half *q, long long q_stride,
                   const __half *kbase, const __half *vbase, long long kv_stride,
                   const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
@@ -112,7 +113,7 @@ int gpt2_attention_b200_batched(gpt2_half *att, const gpt2_half *qkv, int B, int
     if (rc != GPT2_B200_OK || B == 0 || T == 0) return rc;
     if (qkv_seq_stride == 0) qkv_seq_stride = static_cast<long long>(T) * 3 * E;
     if (att_seq_stride == 0) att_seq_stride = static_cast<long long>(T) * E;
-    return launch_prefill(att, qkv, B, T, E, H, qkv_seq_stride, att_seq_stride, stream);
+    return launch_prefill(att, qkv, B, T, E, H, qkv_seq_stride, att_seq_stride, nullptr, 0, stream);
 }
 
 int gpt2_attention_b200_stream(gpt2_half *att, const gpt2_half *qkv, int T, int E, int H, int D,
@@ -122,6 +123,23 @@ int gpt2_attention_b200_stream(gpt2_half *att, const gpt2_half *qkv, int T, int 
 
 void gpt2_attention_b200(gpt2_half *att, const gpt2_half *qkv, int T, int E, int H, int D) {
     set_last_error(gpt2_attention_b200_batched(att, qkv, 1, T, E, H, D, 0, 0, 0));
+}
+
+int gpt2_attention_kv_b200_stream(gpt2_half *att, const gpt2_half *qkv, const GPT2KVCache *kv, int L,
+                                  int T, int E, int H, int D, cudaStream_t stream) {
+    int rc = check_prefill(att, qkv, 1, T, E, H, D, 0, 0);
+    if (rc != GPT2_B200_OK) return rc;
+    if (check_cache(kv) != GPT2_B200_OK || L < 0 || L >= kv->nLayer || kv->nHead != H || T > kv->maxT)
+        return GPT2_B200_EINVAL;
+    if (T == 0) return GPT2_B200_OK;
+    __half *layer = reinterpret_cast<__half *>(kv->data) + static_cast<size_t>(2 * L) * H * kv->maxT * D;
+    return launch_prefill(att, qkv, 1, T, E, H, static_cast<long long>(T) * 3 * E,
+                          static_cast<long long>(T) * E, layer, kv->maxT, stream);
+}
+
+void gpt2_attention_kv_b200(gpt2_half *att, const gpt2_half *qkv, const GPT2KVCache *kv, int L, int T,
+                            int E, int H, int D) {
+    set_last_error(gpt2_attention_kv_b200_stream(att, qkv, kv, L, T, E, H, D, 0));
 }
 
 // ================================================================ decode

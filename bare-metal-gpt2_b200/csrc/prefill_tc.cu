@@ -106,6 +106,7 @@ struct Params {
     int total_items;           // units_per_hb * H * B
     float scale_log2;          // log2(e) / sqrt(D)
     float *part;               // split units: partials [group][chunk][PART_COLS][128 rows]
+    int kv_fill;               // also write K/V rows 0..T-1 into a KV-cache layer (B == 1)
     unsigned *counters;        // split units: arrivals per [group][lane quarter], re-armed to 0
     unsigned *status;
     unsigned long long timeout_ns;
@@ -201,21 +202,39 @@ __device__ __forceinline__ bool aborted(Bars *bars) {
 // stages are released when their QKs complete and V stages when their PVs complete (later), so
 // issuing V one tile behind K keeps the K loads from queueing behind a V wait.
 template <bool kSplit>
-__device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, const Params &p) {
+__device__ void run_producer(const CUtensorMap *tm, const CUtensorMap *tm_kv, uint8_t *smem, Bars *bars,
+                             const Params &p) {
     const unsigned long long to = p.timeout_ns;
     int last_q[NQ] = {-1, -1}, last_k[NSTAGE], last_v[NSTAGE];
-    for (int s = 0; s < NSTAGE; ++s) last_k[s] = last_v[s] = -1;
+    // KV-cache fill: the K/V tile each stage holds that this CTA must also store into the cache
+    // (head << 16 | tile), -1 for none. A tile is stored by the unit of the pair whose top two tiles
+    // it is (tiles 2p and 2p+1 are loaded by no lower pair), so each tile is written exactly once. It
+    // is stored when its stage is about to be reused (it has landed and been consumed) or at teardown.
+    int own_k[NSTAGE], own_v[NSTAGE];
+    for (int s = 0; s < NSTAGE; ++s) last_k[s] = last_v[s] = own_k[s] = own_v[s] = -1;
     bool ok = true;
     Cursor<kSplit> kc, vc;  // next K tile to load; next V tile to load (never ahead of kc)
     kc.start(p);
     vc.start(p);
+    auto owned = [&](const Cursor<kSplit> &c) -> int {
+        const int tile = c.I.kv0 + c.j;
+        return (p.kv_fill && tile >= 2 * c.I.pair) ? (c.I.h << 16) | tile : -1;
+    };
+    // z = head for K, nHead + head for V (the layer's K block is followed by its V block)
+    auto store_tile = [&](const uint8_t *src, int own, int zoff) {
+        tma_store_3d(tm_kv, src, 0, (own & 0xffff) * BN, zoff + (own >> 16));
+        bulk_commit_group();
+        bulk_wait_group_read0();  // the stage may be overwritten once the store has read it
+    };
     auto load_v = [&]() -> bool {
         const int s = vc.g % NSTAGE;
         if (vc.g >= NSTAGE && !mbar_wait(&bars->v_empty[s], ((vc.g / NSTAGE) - 1) & 1, to)) return false;
+        if (own_v[s] >= 0) store_tile(smem + OFF_V + s * TILE_BYTES, own_v[s], p.H);
         mbar_arrive_expect_tx(&bars->v_full[s], TILE_BYTES);
         tma_load_3d(smem + OFF_V + s * TILE_BYTES, tm, &bars->v_full[s], 2 * p.E + vc.I.h * HD,
                     (vc.I.kv0 + vc.j) * BN, vc.I.b);
         last_v[s] = vc.g;
+        own_v[s] = owned(vc);
         vc.advance(p);
         return true;
     };
@@ -237,10 +256,12 @@ __device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, c
         const int s = kc.g % NSTAGE;
         if (kc.g >= NSTAGE && !(ok = mbar_wait(&bars->k_empty[s], ((kc.g / NSTAGE) - 1) & 1, to)))
             break;
+        if (own_k[s] >= 0) store_tile(smem + OFF_K + s * TILE_BYTES, own_k[s], 0);
         mbar_arrive_expect_tx(&bars->k_full[s], TILE_BYTES);
         tma_load_3d(smem + OFF_K + s * TILE_BYTES, tm, &bars->k_full[s], p.E + kc.I.h * HD,
                     (kc.I.kv0 + kc.j) * BN, kc.I.b);
         last_k[s] = kc.g;
+        own_k[s] = owned(kc);
         kc.advance(p);
         if (vc.g + 1 < kc.g && !(ok = load_v())) break;  // V one tile behind K
     }
@@ -255,6 +276,15 @@ __device__ void run_producer(const CUtensorMap *tm, uint8_t *smem, Bars *bars, c
         if (last_v[s] >= 0) drained = mbar_wait(&bars->v_full[s], (last_v[s] / NSTAGE) & 1, to) && drained;
     }
     if (!drained) atomicOr(p.status, ST_PREFILL_DRAIN_TIMEOUT);
+    if (p.kv_fill) {  // the owned tiles still in the rings (their loads have landed)
+        if (drained && !aborted(bars)) {
+            for (int s = 0; s < NSTAGE; ++s) {
+                if (own_k[s] >= 0) store_tile(smem + OFF_K + s * TILE_BYTES, own_k[s], 0);
+                if (own_v[s] >= 0) store_tile(smem + OFF_V + s * TILE_BYTES, own_v[s], p.H);
+            }
+        }
+        bulk_wait_group0();  // cache writes complete before the CTA's shared memory goes away
+    }
 }
 
 // ------------------------------------------------------------------ MMA issuers (one thread per query tile)
@@ -637,8 +667,8 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
 
 template <bool kSplit>
 __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
-    k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv,
-                       const __grid_constant__ CUtensorMap tm_att, const Params p) {
+    k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_att,
+                       const __grid_constant__ CUtensorMap tm_kv, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -671,6 +701,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
         tma_prefetch_desc(&tm_att);
+        if (p.kv_fill) tma_prefetch_desc(&tm_kv);
     }
     if (warp == 1) {
         tmem_alloc(&bars->tmem_base, TMEM_COLS);
@@ -682,7 +713,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     const uint32_t tbase = bars->tmem_base;
 
     if (warp == 0) {
-        if (lane == 0) run_producer<kSplit>(&tm_qkv, smem, bars, p);
+        if (lane == 0) run_producer<kSplit>(&tm_qkv, &tm_kv, smem, bars, p);
         __syncwarp();
     } else if (warp == 1 || warp == MMA_B_WARP) {
         if (lane == 0) run_mma<kSplit>(smem, bars, p, tbase, warp == 1 ? 0 : 1);
@@ -811,7 +842,8 @@ static bool ensure_prefill_workspace(DeviceContext *ctx, size_t floats, size_t w
 
 // Launches the batched causal prefill. Arguments are validated by the caller (api.cu).
 int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
-                   long long qkv_seq_stride, long long att_seq_stride, cudaStream_t stream) {
+                   long long qkv_seq_stride, long long att_seq_stride, __half *kv_layer, int kv_maxT,
+                   cudaStream_t stream) {
     using namespace prefill;
     DeviceContext *ctx = device_context();
     if (!ctx) return GPT2_B200_ECUDA;
@@ -858,7 +890,25 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
         remember_map(1, att, E, T, B, att_seq_stride, ctx->device, tm_att);
     }
 
+    // KV-cache layer (optional, B == 1): K block [H][maxT][64] then V block, rows 0..T-1 written
+    CUtensorMap tm_kv = tm_att;  // unused unless kv_layer is set
+    if (kv_layer) {
+        if (B != 1 || kv_maxT < T) return GPT2_B200_EINVAL;
+        if (!cached_map(2, kv_layer, E, T, kv_maxT, 0, ctx->device, &tm_kv)) {
+            const cuuint64_t kdims[3] = {HD, static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(2 * H)};
+            const cuuint64_t kstrides[2] = {HD * 2, static_cast<cuuint64_t>(kv_maxT) * HD * 2};
+            const cuuint32_t kbox[3] = {HD, BN, 1};
+            const cuuint32_t estr[3] = {1, 1, 1};
+            if (enc(&tm_kv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, kv_layer, kdims, kstrides, kbox, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return GPT2_B200_EINVAL;
+            remember_map(2, kv_layer, E, T, kv_maxT, 0, ctx->device, tm_kv);
+        }
+    }
+
     Params p;
+    p.kv_fill = kv_layer != nullptr;
     p.T = T;
     p.H = H;
     p.E = E;
@@ -899,9 +949,9 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     const long long slots = static_cast<long long>(CTAS_PER_SM) * (ctx->num_sms > 0 ? ctx->num_sms : 148);
     const unsigned grid = static_cast<unsigned>(total < slots ? total : slots);
     if (p.units_per_hb != p.n_pairs)
-        k_flash_prefill_tc<true><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, p);
+        k_flash_prefill_tc<true><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, tm_kv, p);
     else
-        k_flash_prefill_tc<false><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, p);
+        k_flash_prefill_tc<false><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, tm_kv, p);
     return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 

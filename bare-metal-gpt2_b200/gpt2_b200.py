@@ -59,6 +59,8 @@ _SIGS = {
     "gpt2_attention_b200": (None, [_vp, _vp, _ci, _ci, _ci, _ci]),
     "gpt2_attention_b200_stream": (_ci, [_vp, _vp, _ci, _ci, _ci, _ci, _vp]),
     "gpt2_attention_b200_batched": (_ci, [_vp, _vp, _ci, _ci, _ci, _ci, _ci, _cll, _cll, _vp]),
+    "gpt2_attention_kv_b200": (None, [_vp, _vp, _kvp, _ci, _ci, _ci, _ci, _ci]),
+    "gpt2_attention_kv_b200_stream": (_ci, [_vp, _vp, _kvp, _ci, _ci, _ci, _ci, _ci, _vp]),
     "gpt2_attn_decode_b200": (None, [_vp, _vp, _kvp, _ci, _ci]),
     "gpt2_attn_decode_b200_stream": (_ci, [_vp, _vp, _kvp, _ci, _ci, _vp]),
     "gpt2_attn_decode_b200_layers": (_ci, [_vp, _cll, _vp, _cll, _kvp, _ci, _ci, _vp, _ci, _ci, _vp]),

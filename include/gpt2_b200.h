@@ -86,6 +86,18 @@ void gpt2_attention_b200(gpt2_half *att, const gpt2_half *qkv, int T, int E, int
 int gpt2_attention_b200_stream(gpt2_half *att, const gpt2_half *qkv, int T, int E, int H, int D,
                                cudaStream_t stream);
 
+/* Prefill attention that also fills the KV cache: the same att as gpt2_attention_b200, and rows
+ * 0..T-1 of layer L of kv (K and V of every head) written exactly as gpt2_kv_scatter_prefill(kv, L,
+ * qkv, T) writes them (cuda/kvcache.cu:67-81); rows >= T are left untouched and kv->len is not changed.
+ * Replaces the reference's pair of calls in a prefill forward (cuda/forward_cuda.cu:97-98) with one
+ * launch: the K/V tiles the attention loads anyway are stored to the cache from shared memory, so K
+ * and V are read once. Requires kv->nHead == H and T <= kv->maxT. Additive extension; the reference
+ * has no fused counterpart. */
+void gpt2_attention_kv_b200(gpt2_half *att, const gpt2_half *qkv, const GPT2KVCache *kv, int L, int T,
+                            int E, int H, int D);
+int gpt2_attention_kv_b200_stream(gpt2_half *att, const gpt2_half *qkv, const GPT2KVCache *kv, int L,
+                                  int T, int E, int H, int D, cudaStream_t stream);
+
 /* Batched prefill: B independent sequences (or layers) in one launch. Sequence b reads
  * qkv + b*qkv_seq_stride and writes att + b*att_seq_stride (strides in elements; 0 = dense,
  * i.e. T*3E and T*E). Additive extension of cuda/kernels.cuh:73 for batch > 1. */

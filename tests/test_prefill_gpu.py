@@ -125,3 +125,50 @@ def test_large_scores_stay_finite(cuda, lib, oracle):
     lib.prefill(att, dev16(cuda, x), T)
     cuda.cuda.synchronize()
     assert_close(host(att), oracle.prefill(x), "large scores")
+
+
+@pytest.mark.parametrize("T", [1, 129, 300, 1024])
+def test_attention_with_kv_fill_matches_scatter_then_attention(cuda, lib, ref_gpu, T):
+    """gpt2_attention_kv_b200_stream = the reference's gpt2_kv_scatter_prefill followed by attention
+    (cuda/forward_cuda.cu:97-98), bit-exact: att equals the plain prefill's, and the whole cache arena
+    equals the one the reference's own k_kv_scatter writes (rows >= T and other layers untouched).
+    T = 1024 on one layer takes the split-unit path; the others keep whole pairs."""
+    import ctypes
+    import gpt2_b200 as G
+    torch = cuda
+    maxt, n_layer = 1024, 12
+    x = O.seeded_qkv(900 + T, T)
+    d_qkv = dev16(torch, x)
+    mine = torch.full((n_layer, 2, O.H, maxt, O.D), -3.0, dtype=torch.float16, device="cuda")
+    ref = mine.clone()
+    kv = G.cache_view(mine.data_ptr(), n_layer, maxt)
+    att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
+    plain = torch.empty_like(att)
+    for L in (0, 11):
+        rc = lib.gpt2_attention_kv_b200_stream(att.data_ptr(), d_qkv.data_ptr(), ctypes.byref(kv), L, T,
+                                               O.E, O.H, O.D, None)
+        assert rc == 0
+        ref_gpu.kv_scatter_prefill(ref.data_ptr(), maxt, L, d_qkv.data_ptr(), T)
+        lib.prefill(plain, d_qkv, T)
+        torch.cuda.synchronize()
+        assert torch.equal(att.view(torch.int16), plain.view(torch.int16))
+    assert torch.equal(mine.view(torch.int16), ref.view(torch.int16))
+    assert lib.status() == 0
+
+
+def test_attention_with_kv_fill_rejects_bad_cache(cuda, lib):
+    import ctypes
+    import gpt2_b200 as G
+    torch = cuda
+    T, maxt = 300, 256
+    d_qkv = torch.zeros((T, O.QKV), dtype=torch.float16, device="cuda")
+    arena = torch.zeros((12, 2, O.H, maxt, O.D), dtype=torch.float16, device="cuda")
+    att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
+    kv = G.cache_view(arena.data_ptr(), 12, maxt)
+    # T beyond the cache's maxT, and a layer past nLayer: refused, nothing launched
+    assert lib.gpt2_attention_kv_b200_stream(att.data_ptr(), d_qkv.data_ptr(), ctypes.byref(kv), 0, T,
+                                             O.E, O.H, O.D, None) == G.EINVAL
+    kv2 = G.cache_view(arena.data_ptr(), 12, maxt)
+    assert lib.gpt2_attention_kv_b200_stream(att.data_ptr(), d_qkv.data_ptr(), ctypes.byref(kv2), 12, 100,
+                                             O.E, O.H, O.D, None) == G.EINVAL
+    assert lib.status() == 0
