@@ -108,13 +108,41 @@ __global__ void __launch_bounds__(NT) k_decode_stream(const Params p) {
     K += static_cast<long long>(h) * p.maxT * HD;
     V += static_cast<long long>(h) * p.maxT * HD;
 
-    if (t == 0) {
+    // The producer sets up the barriers and issues the first ring of copies before the block-wide
+    // barrier; the consumers meanwhile bring their query into registers.
+    const int first = min(nstages, NSTAGE);
+    if (warp == NCW && lane == 0) {
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], NCW);
         }
         bars->abort = 0;
         fence_mbar_init();
+        for (int i = 0; i < first; ++i) {
+            const int key = k0 + i * KPS;
+            const uint32_t bytes = static_cast<uint32_t>(min(KPS, k1 - key)) * ROW_BYTES;
+            mbar_arrive_expect_tx(&bars->full[i], 2 * bytes);
+            bulk_load(smem + OFF_K + i * STAGE_BYTES, K + static_cast<long long>(key) * HD, bytes, &bars->full[i]);
+            bulk_load(smem + OFF_V + i * STAGE_BYTES, V + static_cast<long long>(key) * HD, bytes, &bars->full[i]);
+        }
+    }
+    const int kq = lane >> 2;        // key of this warp's 8 handled by this lane group
+    const int dq = (lane & 3) * 16;  // 16 dims of that key handled by this lane
+    float qv[16];
+    if (warp < NCW) {
+        const uint4 *q4 = reinterpret_cast<const uint4 *>(p.q + job * p.q_stride + h * HD + dq);
+        const uint4 a = q4[0], b = q4[1];
+        const __half2 *h2a = reinterpret_cast<const __half2 *>(&a);
+        const __half2 *h2b = reinterpret_cast<const __half2 *>(&b);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 fa = __half22float2(h2a[i]);
+            const float2 fb = __half22float2(h2b[i]);
+            qv[2 * i] = fa.x * p.scale_log2;
+            qv[2 * i + 1] = fa.y * p.scale_log2;
+            qv[8 + 2 * i] = fb.x * p.scale_log2;
+            qv[8 + 2 * i + 1] = fb.y * p.scale_log2;
+        }
     }
     __syncthreads();
 
@@ -122,8 +150,8 @@ __global__ void __launch_bounds__(NT) k_decode_stream(const Params p) {
         // ------------------------------------------------------------ producer (one thread)
         if (lane == 0) {
             bool ok = true;
-            int issued = 0;
-            for (int i = 0; i < nstages; ++i) {
+            int issued = first;
+            for (int i = first; i < nstages; ++i) {
                 const int s = i % NSTAGE;
                 if (i >= NSTAGE) {
                     ok = mbar_wait(&bars->empty[s], ((i / NSTAGE) - 1) & 1, to);
@@ -152,24 +180,6 @@ __global__ void __launch_bounds__(NT) k_decode_stream(const Params p) {
         __syncwarp();
     } else {
         // ------------------------------------------------------------ consumers (8 warps)
-        const int kq = lane >> 2;        // key of this warp's 8 handled by this lane group
-        const int dq = (lane & 3) * 16;  // 16 dims of that key handled by this lane
-        float qv[16];
-        {
-            const uint4 *q4 = reinterpret_cast<const uint4 *>(p.q + job * p.q_stride + h * HD + dq);
-            const uint4 a = q4[0], b = q4[1];
-            const __half2 *h2a = reinterpret_cast<const __half2 *>(&a);
-            const __half2 *h2b = reinterpret_cast<const __half2 *>(&b);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 fa = __half22float2(h2a[i]);
-                const float2 fb = __half22float2(h2b[i]);
-                qv[2 * i] = fa.x * p.scale_log2;
-                qv[2 * i + 1] = fa.y * p.scale_log2;
-                qv[8 + 2 * i] = fb.x * p.scale_log2;
-                qv[8 + 2 * i + 1] = fb.y * p.scale_log2;
-            }
-        }
         float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;  // o: dims 2*lane, 2*lane+1
         bool ok = true;
         for (int i = 0; i < nstages; ++i) {
