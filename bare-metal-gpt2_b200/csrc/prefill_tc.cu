@@ -524,13 +524,15 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
             for (int cb = 0; cb < 4; ++cb) {
                 uint32_t pk[16];
                 exp_chunk(cb, pk);
+                if (cb == 3) {  // last exponentials computed: the other warp may take the MUFU
+                    ++ex2_phases;
+                    if (lane == 0)  // (the value depends on the last ex2, so it is not stored earlier)
+                        *reinterpret_cast<volatile int *>(&S.ex2_done[quarter]) =
+                            ex2_phases + (pk[15] == 0xFFFFFFFFu ? 1 : 0);
+                }
                 tmem_st16(tP + 16 * cb, pk);
             }
             l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-            __syncwarp();
-            ++ex2_phases;
-            if (lane == 0)  // the other query tile's warp on this sub-partition may go
-                *reinterpret_cast<volatile int *>(&S.ex2_done[quarter]) = ex2_phases;
             if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll
                 for (int cb = 0; cb < 2; ++cb) {

@@ -172,3 +172,21 @@ def test_attention_with_kv_fill_rejects_bad_cache(cuda, lib):
     assert lib.gpt2_attention_kv_b200_stream(att.data_ptr(), d_qkv.data_ptr(), ctypes.byref(kv2), 12, 100,
                                              O.E, O.H, O.D, None) == G.EINVAL
     assert lib.status() == 0
+
+
+@pytest.mark.parametrize("T", [1400, 2048, 4096])
+def test_single_layer_long_prompts_split_path(cuda, lib, oracle, T):
+    """One layer of one long sequence: too few whole pairs to fill the SMs, so the key ranges of the
+    long query tiles are split across CTAs and merged (an odd tile count at T=1400 leaves a pair with
+    query tile A only; T=4096 reaches the cap of 8 chunks per pair). Checked against the oracle on a
+    sample of rows across the range, plus the last row."""
+    torch = cuda
+    x = O.seeded_qkv(4000 + T, T)
+    att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
+    lib.prefill(att, dev16(torch, x), T)
+    torch.cuda.synchronize()
+    assert lib.status() == 0
+    got = host(att)
+    rows = sorted(set(list(range(0, T, 97)) + [T - 1]))
+    ref = oracle.prefill(x)
+    assert_close(got[rows], ref[rows], f"T={T} sampled rows vs oracle")
