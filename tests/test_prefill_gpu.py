@@ -190,3 +190,37 @@ def test_single_layer_long_prompts_split_path(cuda, lib, oracle, T):
     rows = sorted(set(list(range(0, T, 97)) + [T - 1]))
     ref = oracle.prefill(x)
     assert_close(got[rows], ref[rows], f"T={T} sampled rows vs oracle")
+
+
+def test_single_layer_prefill_in_cuda_graph(cuda, lib, oracle):
+    """A one-layer launch takes the split-unit path, whose workspace is never allocated during stream
+    capture: captured before any eager call it keeps whole pairs, captured after one it replays the
+    split path. Both graphs must reproduce the eager result across replays."""
+    torch = cuda
+    T = 1024
+    x = O.seeded_qkv(5150, T)
+    d_qkv = dev16(torch, x)
+    ref = oracle.prefill(x)
+    s = torch.cuda.Stream()
+    outs = []
+    for _ in range(2):  # first capture may predate the workspace; the eager call below creates it
+        att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
+        g = torch.cuda.CUDAGraph()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(g, stream=s):
+            rc = lib.gpt2_attention_b200_stream(att.data_ptr(), d_qkv.data_ptr(), T, O.E, O.H, O.D,
+                                                s.cuda_stream)
+            assert rc == 0
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            att.fill_(0)
+            g.replay()
+            torch.cuda.synchronize()
+            assert_close(host(att), ref, "graph-replayed one-layer prefill")
+        outs.append(att.clone())
+        eager = torch.empty_like(att)
+        lib.prefill(eager, d_qkv, T)
+        torch.cuda.synchronize()
+        outs.append(eager)
+        del g
+    assert lib.status() == 0
