@@ -98,6 +98,8 @@ static_assert(sizeof(Bars) <= 512, "barrier block");
 
 struct Params {
     int T, H, E, B;
+    unsigned hb_magic, h_magic;  // magic multipliers: item index / (H * B) and / H without division
+    int hb_shift, h_shift;
     int n_qtiles;
     int n_pairs;               // ceil(n_qtiles / 2)
     int kv_chunk;              // K/V tiles per work unit (>= n_qtiles: a pair is never split)
@@ -124,6 +126,15 @@ struct Item {
     __device__ __forceinline__ int nk_of(int x) const { return x ? nk[1] : nk[0]; }
 };
 
+// n / d for any 32-bit unsigned n and 1 <= d < 2^31 with a precomputed magic (round-up method:
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1; q = (t + ((n - t) >> 1)) >> (l - 1) with
+// t = mulhi(m, n); d == 1 is passed through).
+__device__ __forceinline__ unsigned div_magic(unsigned n, unsigned d, unsigned m, int l) {
+    if (d == 1) return n;
+    const unsigned t = __umulhi(m, n);
+    return (t + ((n - t) >> 1)) >> (l - 1);
+}
+
 // K/V tiles a pair's key range covers: through B's diagonal, or A's when B is past T.
 __device__ __forceinline__ int pair_kv_tiles(const Params &p, int pair) {
     return (2 * pair + 1 < p.n_qtiles) ? 2 * pair + 2 : 2 * pair + 1;
@@ -140,10 +151,10 @@ __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
     if (i >= p.total_items) return false;
     const int per = p.H * p.B;
     const int idx = static_cast<int>(i);
-    int u = idx / per;  // unit within its (head, sequence)
-    const int rem = idx % per;
-    it.h = rem % p.H;
-    it.b = rem / p.H;
+    int u = static_cast<int>(div_magic(idx, per, p.hb_magic, p.hb_shift));  // unit in its (head, seq)
+    const int rem = idx - u * per;
+    it.b = static_cast<int>(div_magic(rem, p.H, p.h_magic, p.h_shift));
+    it.h = rem - it.b * p.H;
     int pr = p.n_pairs - 1 - u, nc = 1;  // whole pairs: unit u is pair n_pairs-1-u, one chunk
     if (kSplit) {
         for (pr = p.n_pairs - 1; pr > 0; --pr) {
@@ -575,16 +586,17 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
         bool store = true;  // this warp holds the final rows of its 32 queries
         if (!kSplit || I.nchunk == 1) {
             const float inv_l = 1.f / l;
+            uint32_t v[2][32];  // both halves of the row in flight before one wait
+            tmem_ld32(tO, v[0]);
+            tmem_ld32(tO + 32, v[1]);
+            tmem_wait_ld();
 #pragma unroll
             for (int cb = 0; cb < 2; ++cb) {  // 32 columns of O at a time
-                uint32_t v[32];
-                tmem_ld32(tO + 32 * cb, v);
-                tmem_wait_ld();
                 uint32_t o[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
-                    o[i] = pack_half2(__uint_as_float(v[2 * i]) * inv_l,
-                                      __uint_as_float(v[2 * i + 1]) * inv_l);
+                    o[i] = pack_half2(__uint_as_float(v[cb][2 * i]) * inv_l,
+                                      __uint_as_float(v[cb][2 * i + 1]) * inv_l);
                 put32(cb, o);
             }
             tc_fence_before();
@@ -916,6 +928,15 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     Params p;
     p.kv_fill = kv_layer != nullptr;
     p.T = T;
+    auto magic = [](unsigned d, unsigned *m, int *l) {
+        int sh = 0;
+        while ((1ull << sh) < d) ++sh;
+        *m = static_cast<unsigned>((((1ull << 32) * ((1ull << sh) - d)) / d + 1) & 0xffffffffull);
+        *l = sh;
+    };
+    if (static_cast<long long>(H) * B >= (1ll << 31)) return GPT2_B200_EINVAL;
+    magic(static_cast<unsigned>(H * B), &p.hb_magic, &p.hb_shift);
+    magic(static_cast<unsigned>(H), &p.h_magic, &p.h_shift);
     p.H = H;
     p.E = E;
     p.B = B;
