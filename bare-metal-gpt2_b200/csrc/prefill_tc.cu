@@ -632,18 +632,27 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
             if (store) {  // last chunk of these 32 rows: merge every chunk's partial row
                 __threadfence();
                 const float *base = p.part + grp * p.max_chunks * (PART_COLS * BM) + row;
-                float mk[MAX_CHUNKS], w[MAX_CHUNKS];
-                float M = -INFINITY;
+                constexpr int CH = PART_COLS * BM;  // floats per chunk
+                // Loads are predicated rather than branched so that each batch is one L2 round trip:
+                // (m, l) of every chunk, then per 32-column half up to 4 chunks' values at once.
+                float mk[MAX_CHUNKS], lk[MAX_CHUNKS], w[MAX_CHUNKS];
 #pragma unroll
                 for (int k = 0; k < MAX_CHUNKS; ++k) {
-                    mk[k] = k < ncx ? __ldcg(base + k * (PART_COLS * BM) + HD * BM) : -INFINITY;
-                    M = fmaxf(M, mk[k]);
+                    mk[k] = -INFINITY;
+                    lk[k] = 0.f;
+                    if (k < ncx) {
+                        mk[k] = __ldcg(base + k * CH + HD * BM);
+                        lk[k] = __ldcg(base + k * CH + (HD + 1) * BM);
+                    }
                 }
+                float M = -INFINITY;
+#pragma unroll
+                for (int k = 0; k < MAX_CHUNKS; ++k) M = fmaxf(M, k < ncx ? mk[k] : -INFINITY);
                 float L = 0.f;
 #pragma unroll
                 for (int k = 0; k < MAX_CHUNKS; ++k) {
                     w[k] = k < ncx ? ex2_approx(mk[k] - M) : 0.f;
-                    if (k < ncx) L = fmaf(w[k], __ldcg(base + k * (PART_COLS * BM) + (HD + 1) * BM), L);
+                    L = fmaf(w[k], lk[k], L);
                 }
                 const float inv_l = 1.f / L;
 #pragma unroll
@@ -652,12 +661,25 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
 #pragma unroll
                     for (int i = 0; i < 32; ++i) acc[i] = 0.f;
 #pragma unroll
-                    for (int k = 0; k < MAX_CHUNKS; ++k)
-                        if (k < ncx) {
-                            const float *pc = base + k * (PART_COLS * BM) + (32 * cb) * BM;
+                    for (int k0 = 0; k0 < MAX_CHUNKS; k0 += 4) {
+                        if (k0 < ncx) {
+                            float vals[4][32];
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) acc[i] = fmaf(w[k], __ldcg(pc + i * BM), acc[i]);
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const float *pc = base + (k0 + kk) * CH + (32 * cb) * BM;
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) vals[kk][i] = 0.f;
+                                if (k0 + kk < ncx) {
+#pragma unroll
+                                    for (int i = 0; i < 32; ++i) vals[kk][i] = __ldcg(pc + i * BM);
+                                }
+                            }
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) acc[i] = fmaf(w[k0 + kk], vals[kk][i], acc[i]);
                         }
+                    }
                     uint32_t o[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) o[i] = pack_half2(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
