@@ -28,9 +28,15 @@
 //                        P values (numerator and denominator use identical weights); O is rescaled in
 //                        TMEM only when the running max grows by more than 2^8 (the stale max is
 //                        otherwise kept for both l and O: exact, and P <= 256). The A and B warps that
-//                        share an SM sub-partition take turns on its MUFU (ex2) pipe. Epilogue: O / l ->
-//                        fp16 -> a swizzled 4 KB shared-memory slot per warp -> one TMA store of the
-//                        warp's 32 rows, so output rows leave as whole 128-byte lines.
+//                        share an SM sub-partition take turns on its MUFU (ex2) pipe (A may run one
+//                        turn ahead). Epilogue: O / l -> fp16 -> a swizzled 4 KB shared-memory slot per
+//                        warp -> one TMA store of the warp's 32 rows, so output rows leave as whole
+//                        128-byte lines.
+//
+// Launches with fewer whole pairs than SMs (one layer of one sequence) run the kSplit instantiation: a
+// work unit is a chunk of a pair's key range; split units park unnormalised rows (o, m, l) in a
+// workspace and the last chunk to arrive for a 32-row group merges them. With a KV-cache target the
+// producer also stores the K/V tiles its unit owns into the cache, straight from the ring.
 //
 // TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 224.5 KB
 // (Q 64 KB, K and V rings 128 KB, output slots 32 KB, barriers). No cluster, no multicast. Every
