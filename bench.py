@@ -463,6 +463,8 @@ def main(argv=None):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # stdout carries exactly one JSON line: NCCL's own log (version banner included) goes to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import gpt2_b200 as G
