@@ -20,6 +20,8 @@ enum StatusBits : unsigned {
     ST_DECODE_BAD_LEN = 1u << 8,           // device-side length outside [1, maxT]
     ST_DECODE_TIMEOUT = 1u << 10,          // a decode stage wait gave up
     ST_KV_BAD_POS = 1u << 9,               // device-side append position outside [0, maxT)
+    ST_LINEAR_TIMEOUT = 1u << 11,          // a batched linear layer's stage wait gave up
+    ST_MODEL_BAD_TOKEN = 1u << 12,         // a token id outside [0, vocab) reached the embedding
     ST_TEST_WAIT_TIMEOUT = 1u << 16,       // the wait-timeout self-test expired (expected)
 };
 

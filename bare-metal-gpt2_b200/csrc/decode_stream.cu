@@ -87,6 +87,10 @@ __global__ void __launch_bounds__(NT) k_decode_stream(const Params p) {
     const int split = blockIdx.x, h = blockIdx.y, job = blockIdx.z;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const unsigned long long to = p.timeout_ns;
+    // Launched as a programmatic dependent (the batched decode step), the grid may start while its
+    // predecessor finishes; nothing it reads is touched before the predecessor has completed.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     int len = p.len;
     if (p.d_len) len = (p.len_per_job ? p.d_len[job] : p.d_len[0]) + p.len_add;
@@ -329,11 +333,9 @@ int decode_stream_splits(int max_len, long long pairs, int num_sms) {
     return static_cast<int>(n);
 }
 
-int launch_decode_stream(__half *out, long long out_stride, const __half *q, long long q_stride,
-                         const __half *kbase, const __half *vbase, long long kv_stride,
-                         const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
-                         int len_per_job, int len_add, int len, int max_len, int njobs, int H,
-                         int maxT, cudaStream_t stream) {
+// Sets the kernel's shared-memory attribute on the current device (once), so that a later launch
+// inside a stream capture makes no configuration call.
+int prepare_decode_stream() {
     DeviceContext *ctx = device_context();
     if (!ctx) return GPT2_B200_ECUDA;
     if (!ctx->decode_attr_done) {
@@ -342,6 +344,17 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
             return GPT2_B200_ECUDA;
         ctx->decode_attr_done = true;
     }
+    return GPT2_B200_OK;
+}
+
+int launch_decode_stream(__half *out, long long out_stride, const __half *q, long long q_stride,
+                         const __half *kbase, const __half *vbase, long long kv_stride,
+                         const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
+                         int len_per_job, int len_add, int len, int max_len, int njobs, int H,
+                         int maxT, cudaStream_t stream, bool pdl) {
+    DeviceContext *ctx = device_context();
+    if (!ctx) return GPT2_B200_ECUDA;
+    if (!ctx->decode_attr_done && prepare_decode_stream() != GPT2_B200_OK) return GPT2_B200_ECUDA;
     dstream::Params p;
     p.q = q;
     p.q_stride = q_stride;
@@ -373,9 +386,18 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
         p.part = ctx->part;
         p.counters = ctx->counters;
     }
-    dim3 grid(p.nsplit, H, njobs);
-    dstream::k_decode_stream<<<grid, dstream::NT, dstream::SMEM_BYTES, stream>>>(p);
-    return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.nsplit, H, njobs);
+    cfg.blockDim = dim3(dstream::NT, 1, 1);
+    cfg.dynamicSmemBytes = dstream::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, dstream::k_decode_stream, p) == cudaSuccess ? GPT2_B200_OK
+                                                                                 : GPT2_B200_ECUDA;
 }
 
 }  // namespace b200

@@ -76,6 +76,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     }
 }
 
+// Non-blocking test of a phase.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Same contract as mbar_wait, for a single thread on a latency-critical chain (a pipeline whose
+// stages land just in time): it polls with test_wait instead of letting the thread be suspended,
+// so it resumes within a few cycles of the phase completing. The wall clock is read every 256
+// polls; the bound is the same.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_test_wait(a, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_test_wait(a, parity)) return true;
+        if (globaltimer_ns() - t0 > timeout_ns) return false;
+    }
+}
+
 // Makes generic-proxy writes to shared memory (e.g. P tiles written by threads) visible to the
 // async proxy (TMA, tcgen05.mma operands).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -92,6 +119,16 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+// 2-D tiled load of one box (no multicast); the innermost coordinate c0 is a multiple of 64 halves
+// at every call site.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0,
+                                            int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
         : "memory");
 }
 // Contiguous bulk copy global -> shared (no tensor map, no multicast). dst, src and bytes must be
@@ -170,6 +207,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
           "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
           "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+// Same shape, 16 columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+        " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -275,6 +322,61 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
             smem_u32(bar))
         : "memory");
+}
+
+// ---------------------------------------------------------------- thread-block clusters
+// Rank of this CTA in its cluster (0 for a launch without clusters).
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Hardware barrier over every thread of every CTA in the cluster; release/acquire order the
+// shared-memory writes before it with the distributed shared-memory reads after it. Executed by all
+// threads of each CTA, like __syncthreads.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of cluster_sync_all, for a barrier whose wait comes long after the arrival.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Remote 16-byte store into another CTA's shared memory (cluster address) that signals its bytes
+// on an mbarrier in that CTA (cluster address): the receiver waits on its own barrier, the sender
+// never waits.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_saddr, float4 v, uint32_t cluster_bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+            cluster_saddr),
+        "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cluster_bar)
+        : "memory");
+}
+// Address of the same shared-memory location in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local_saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_saddr) : "memory");
+    return v;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Waits until the grids this one depends on (launched with programmatic stream serialization) have
+// completed and their memory is visible; a no-op for an ordinary launch.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the dependent grid start launching (its CTAs still wait in grid_dependency_wait for this
+// grid's completion before reading what it writes).
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- math

@@ -26,7 +26,24 @@ ST_PREFILL_SMEM_ALIGN = 1 << 3
 ST_PREFILL_DRAIN_TIMEOUT = 1 << 4
 ST_DECODE_BAD_LEN = 1 << 8
 ST_KV_BAD_POS = 1 << 9
+ST_DECODE_TIMEOUT = 1 << 10
+ST_LINEAR_TIMEOUT = 1 << 11
+ST_MODEL_BAD_TOKEN = 1 << 12
 ST_TEST_WAIT_TIMEOUT = 1 << 16
+
+LINEAR_STORE, LINEAR_GELU, LINEAR_RESID = 0, 1, 2
+GEN_ATTENTION_ONLY = 1
+
+# GPT-2-124M (the reference's model/config.h).
+N_LAYER, N_HEAD, N_EMBD, VOCAB, N_CTX = 12, 12, 768, 50257, 1024
+FFN, QKV_DIM = 4 * N_EMBD, 3 * N_EMBD
+# Per-layer tensors in GPT2LayerGPU order (cuda/kernels.cuh:19-23) with their shapes.
+LAYER_TENSORS = (
+    ("ln1_g", (N_EMBD,)), ("ln1_b", (N_EMBD,)), ("qkv_w", (QKV_DIM, N_EMBD)), ("qkv_b", (QKV_DIM,)),
+    ("attn_proj_w", (N_EMBD, N_EMBD)), ("attn_proj_b", (N_EMBD,)), ("ln2_g", (N_EMBD,)),
+    ("ln2_b", (N_EMBD,)), ("fc_w", (FFN, N_EMBD)), ("fc_b", (FFN,)), ("proj_w", (N_EMBD, FFN)),
+    ("proj_b", (N_EMBD,)),
+)
 
 
 class GPT2KVCache(ctypes.Structure):
@@ -53,8 +70,30 @@ class GPT2Backend(ctypes.Structure):
     ]
 
 
+class GPT2LayerGPU(ctypes.Structure):
+    """Same layout as GPT2LayerGPU in the reference's cuda/kernels.cuh:19-23."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n, _ in LAYER_TENSORS]
+
+
+class GPT2WeightsGPU(ctypes.Structure):
+    """Same layout as GPT2WeightsGPU in the reference's cuda/kernels.cuh:41-48."""
+
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("n", ctypes.c_size_t),
+        ("wte", ctypes.c_void_p),
+        ("wpe", ctypes.c_void_p),
+        ("layers", GPT2LayerGPU * N_LAYER),
+        ("lnf_g", ctypes.c_void_p),
+        ("lnf_b", ctypes.c_void_p),
+        ("q", ctypes.c_void_p),
+    ]
+
+
 _vp, _ci, _cll, _cu, _cd = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_uint, ctypes.c_double
 _kvp = ctypes.POINTER(GPT2KVCache)
+_wp = ctypes.POINTER(GPT2WeightsGPU)
 _SIGS = {
     "gpt2_attention_b200": (None, [_vp, _vp, _ci, _ci, _ci, _ci]),
     "gpt2_attention_b200_stream": (_ci, [_vp, _vp, _ci, _ci, _ci, _ci, _vp]),
@@ -77,6 +116,15 @@ _SIGS = {
     "gpt2_kv_append_b200_stream": (_ci, [_kvp, _ci, _ci, _vp, _cll, _vp, _ci, _vp]),
     "gpt2_kv_scatter_prefill_b200": (None, [_kvp, _ci, _vp, _ci]),
     "gpt2_kv_scatter_prefill_b200_stream": (_ci, [_kvp, _ci, _vp, _ci, _vp]),
+    "gpt2_decode_step_b200": (None, [_vp, _wp, _kvp, _ci, _ci, _vp, _vp, _vp]),
+    "gpt2_b200_batch_create": (_ci, [ctypes.POINTER(_vp), _wp, _kvp, _ci]),
+    "gpt2_b200_batch_destroy": (None, [_vp]),
+    "gpt2_b200_batch_step": (_ci, [_vp, _vp, _vp, _vp, _cll, _vp, _vp]),
+    "gpt2_b200_batch_generate": (_ci, [_vp, _vp, _cll, _vp, _ci, _vp, _cll, _ci, _vp]),
+    "gpt2_b200_batch_launches_per_step": (_ci, [_vp, _ci]),
+    "gpt2_b200_linear": (_ci, [_vp, _cll, _vp, _cll, _vp, _vp, _ci, _ci, _ci, _ci, _vp]),
+    "gpt2_b200_linear_argmax": (_ci, [_vp, _cll, _vp, _cll, _vp, _ci, _ci, _ci, _vp, _vp]),
+    "gpt2_gemv_b200": (None, [_vp, _vp, _vp, _vp, _ci, _ci]),
     "gpt2_b200_compose_backend": (None, [ctypes.POINTER(GPT2Backend), ctypes.POINTER(GPT2Backend)]),
     "gpt2_b200_reserve": (_ci, [_ci, _ci, _ci]),
     "gpt2_b200_status": (_cu, [_ci]),
@@ -148,6 +196,61 @@ def cache_view(data_ptr: int, n_layer: int, max_t: int, n_head: int = 12, head_d
     kv.bytes = 2 * n_layer * n_head * max_t * head_dim * 2
     kv.len = length
     return kv
+
+
+class ModelWeights:
+    """Seeded random GPT-2-124M fp16 weights in one device buffer, described by a GPT2WeightsGPU.
+
+    hf_init=True follows GPT-2's initialisation (linear weights and embeddings N(0, std), biases 0,
+    LayerNorm gain 1 and bias 0); hf_init=False also randomises the biases and LayerNorm parameters
+    so that every epilogue term is exercised (tests).
+    """
+
+    def __init__(self, torch, device, seed: int = 0, std: float = 0.02, hf_init: bool = True):
+        shapes = [("wte", (VOCAB, N_EMBD)), ("wpe", (N_CTX, N_EMBD))]
+        shapes += [(f"h{L}.{n}", sh) for L in range(N_LAYER) for n, sh in LAYER_TENSORS]
+        shapes += [("lnf_g", (N_EMBD,)), ("lnf_b", (N_EMBD,))]
+        total = sum(_numel(sh) for _, sh in shapes)
+        self.buf = torch.empty(total, dtype=torch.float16, device=device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.t = {}
+        off = 0
+        for name, sh in shapes:
+            n = _numel(sh)
+            v = self.buf[off:off + n].view(sh)
+            off += n
+            if name.endswith("_g"):
+                v.fill_(1.0)
+                if not hf_init:
+                    v.add_(0.1 * torch.randn(sh, generator=gen, device=device))
+            elif name.endswith("_b"):
+                if hf_init:
+                    v.zero_()
+                else:
+                    v.copy_(std * torch.randn(sh, generator=gen, device=device))
+            else:
+                v.copy_(std * torch.randn(sh, generator=gen, device=device))
+            self.t[name] = v
+        w = GPT2WeightsGPU()
+        w.data = self.buf.data_ptr()
+        w.n = total
+        w.wte = self.t["wte"].data_ptr()
+        w.wpe = self.t["wpe"].data_ptr()
+        for L in range(N_LAYER):
+            for n, _ in LAYER_TENSORS:
+                setattr(w.layers[L], n, self.t[f"h{L}.{n}"].data_ptr())
+        w.lnf_g = self.t["lnf_g"].data_ptr()
+        w.lnf_b = self.t["lnf_b"].data_ptr()
+        w.q = None
+        self.struct = w
+
+
+def _numel(shape) -> int:
+    n = 1
+    for d in shape:
+        n *= d
+    return n
 
 
 _LIB: Lib | None = None

@@ -72,6 +72,28 @@ typedef struct {
     void (*gemv)(void);
     void (*gemv_q)(void);
 } GPT2Backend;
+
+/* fp16 device weights, identical layout to GPT2LayerGPU / GPT2WeightsGPU in cuda/kernels.cuh:19-48
+ * (12 layers; every linear weight [out, in] row-major, model/weights.h:3-5). q is the reference's
+ * optional INT8 attachment; it is not read here. */
+typedef struct {
+    gpt2_half *ln1_g, *ln1_b, *qkv_w, *qkv_b, *attn_proj_w, *attn_proj_b,
+              *ln2_g, *ln2_b, *fc_w, *fc_b, *proj_w, *proj_b;
+} GPT2LayerGPU;
+typedef struct {
+    gpt2_half *data; /* owns the whole fp16 body (device) */
+    size_t n;
+    gpt2_half *wte, *wpe; /* wte is also the tied output head */
+    GPT2LayerGPU layers[12];
+    gpt2_half *lnf_g, *lnf_b;
+    const void *q;
+} GPT2WeightsGPU;
+
+/* Reusable device activation scratch, identical layout to GPT2ScratchGPU (cuda/kernels.cuh:54). */
+typedef struct {
+    gpt2_half *x, *ln, *qkv, *att, *ao, *fc, *ff;
+    int maxT;
+} GPT2ScratchGPU;
 #endif
 
 /* ================================================================ prefill attention */
@@ -182,6 +204,79 @@ int gpt2_kv_append_b200_stream(GPT2KVCache *kv, int L0, int nL, const gpt2_half 
 void gpt2_kv_scatter_prefill_b200(GPT2KVCache *kv, int L, const gpt2_half *qkv, int T);
 int gpt2_kv_scatter_prefill_b200_stream(GPT2KVCache *kv, int L, const gpt2_half *qkv, int T,
                                         cudaStream_t stream);
+
+/* ================================================================ the decode step around attention
+ * The reference's decode step (gpt2_decode_step_cuda, cuda/kvcache.cuh:74-76, cuda/kvcache.cu:233-269)
+ * runs 135 launches per token for ONE sequence: embed, and per layer LayerNorm, QKV GEMV, K/V append,
+ * attention, projection GEMV, add, LayerNorm, FC GEMV, GELU, projection GEMV, add; then the final
+ * LayerNorm and the tied-head GEMV. The entry points below run the same step for B sequences at once:
+ * every weight matmul is one tcgen05 pass over the weights for all B rows with bias, GELU, residual
+ * add and the K/V append fused into its epilogue, the attention is the batched decode kernel above,
+ * and the head's epilogue reduces the logits to per-sequence argmax keys. Four weight launches, one
+ * attention launch and one LayerNorm launch per layer. GPT-2-124M shapes only (E 768, 12 layers,
+ * 12 heads, vocabulary 50257). */
+
+/* Drop-in for gpt2_decode_step_cuda on the fp16 path: consumes `token` at position `pos` of *kv
+ * (kv->len must equal pos), appends every layer's K/V, writes logits[50257] when logits is not NULL
+ * and captures the hidden states into caps_blocks when it is not NULL ((12+2)*768 halves: after
+ * block L at L*768, final LayerNorm at 12*768, embedding at 13*768 — the reference's layout), then
+ * sets kv->len = pos+1. be and s are accepted for signature compatibility and not used: the step's
+ * activations live in a plan the library keeps per (weights, cache) pair, allocated by the first
+ * call for that pair (about 10 KB plus tensor maps). Legacy default stream; errors go to
+ * gpt2_b200_last_error(). */
+void gpt2_decode_step_b200(const GPT2Backend *be, const GPT2WeightsGPU *w, GPT2KVCache *kv, int token,
+                           int pos, GPT2ScratchGPU *s, gpt2_half *logits, gpt2_half *caps_blocks);
+
+/* A batch of B (1..256) sequences decoded together, sequence b over the cache kvs[b] (host array of
+ * B caches in the reference layout, all with the GPT-2-124M shape and the same maxT). Holds its own
+ * activations, tensor maps and launch plans; the weights and caches stay owned by the caller. */
+typedef struct gpt2_b200_batch gpt2_b200_batch;
+int gpt2_b200_batch_create(gpt2_b200_batch **out, const GPT2WeightsGPU *w, const GPT2KVCache *kvs,
+                           int B);
+void gpt2_b200_batch_destroy(gpt2_b200_batch *bt);
+
+/* One decode step: sequence b consumes d_tokens[b] at position d_pos[b] (device ints), appends its
+ * K/V at that position in every layer and attends over d_pos[b]+1 keys. Optional outputs: logits
+ * ([B][logits_stride] halves, the fp16 logits) and d_next (B device ints: argmax of each row, the
+ * first index on ties). Cache len fields are not touched. */
+int gpt2_b200_batch_step(gpt2_b200_batch *bt, const int *d_tokens, const int *d_pos, gpt2_half *logits,
+                         long long logits_stride, int *d_next, cudaStream_t stream);
+
+/* Greedy generation in lock-step, one CUDA graph replay per step: at step t (0 <= t < n_steps) every
+ * sequence consumes its token at position t; the token for position t+1 is d_prompt[b][t+1] while
+ * t+1 < d_plen[b] (the prompt, fed one token per step) and the argmax of step t's logits after that.
+ * d_out[b][0..n_steps] receives every sequence's tokens (prompt and generated; out_stride >=
+ * n_steps+1). n_steps <= maxT. flags: 0, or GPT2_B200_GEN_ATTENTION_ONLY to replay only the
+ * attention launches of each step (same lengths; a timing aid for the attention share). */
+#define GPT2_B200_GEN_ATTENTION_ONLY 1
+int gpt2_b200_batch_generate(gpt2_b200_batch *bt, const int *d_prompt, long long prompt_stride,
+                             const int *d_plen, int n_steps, int *d_out, long long out_stride,
+                             int flags, cudaStream_t stream);
+
+/* The batched linear layer the step is built from (additive; the B-row counterpart of the GEMV slot
+ * GPT2Backend.gemv / gpt2_gemv_fp16, cuda/kernels.cuh:94, cuda/kvcache.cu:212-214):
+ * C[b, n] = epilogue(fp16(sum_k A[b, k] * W[n, k] + bias[n])) for b < B (1..256), W [N, K] row-major,
+ * K a multiple of 64, bias may be NULL. epi: GPT2_B200_LINEAR_STORE writes the value, _GELU writes
+ * gelu_new of it, _RESID adds it to C (the residual add). 16-byte aligned A and W, lda and ldc
+ * multiples of 8. */
+#define GPT2_B200_LINEAR_STORE 0
+#define GPT2_B200_LINEAR_GELU 1
+#define GPT2_B200_LINEAR_RESID 2
+int gpt2_b200_linear(gpt2_half *C, long long ldc, const gpt2_half *A, long long lda,
+                     const gpt2_half *W, const gpt2_half *bias, int B, int N, int K, int epi,
+                     cudaStream_t stream);
+/* The tied-head form: logits[b, n] = fp16(sum_k A[b, k] * W[n, k]) (written when logits is not NULL)
+ * and d_next[b] = the first index of the row's maximum. */
+int gpt2_b200_linear_argmax(gpt2_half *logits, long long ldl, const gpt2_half *A, long long lda,
+                            const gpt2_half *W, int B, int N, int K, int *d_next,
+                            cudaStream_t stream);
+/* Same signature and meaning as gpt2_gemv_fp16 (the GPT2Backend.gemv slot): C[1, N] = A[1, K] W^T + b,
+ * legacy default stream. K must be a multiple of 64 (all GPT-2 weight matmuls). */
+void gpt2_gemv_b200(gpt2_half *C, const gpt2_half *A, const gpt2_half *W, const gpt2_half *bias, int N,
+                    int K);
+
+/* Kernel launches one gpt2_b200_batch_step / one generate step makes (launch accounting). */
+int gpt2_b200_batch_launches_per_step(const gpt2_b200_batch *bt, int flags);
 
 /* ================================================================ backend, status, set-up */
 

@@ -101,8 +101,32 @@ class Oracle:
             raise ValueError("oracle_kv_scatter_u16 rejected its arguments")
 
 
+_LAYER_NAMES = ("ln1_g", "ln1_b", "qkv_w", "qkv_b", "attn_proj_w", "attn_proj_b", "ln2_g", "ln2_b",
+                "fc_w", "fc_b", "proj_w", "proj_b")
+
+
+class _Layer(ctypes.Structure):
+    """GPT2Layer (model/weights.h:8-15): fp32 host pointers."""
+    _fields_ = [(n, ctypes.c_void_p) for n in _LAYER_NAMES]
+
+
+class _Weights(ctypes.Structure):
+    """GPT2Weights (model/weights.h:17-24)."""
+    _fields_ = [("data", ctypes.c_void_p), ("n_floats", ctypes.c_size_t), ("wte", ctypes.c_void_p),
+                ("wpe", ctypes.c_void_p), ("layers", _Layer * 12), ("lnf_g", ctypes.c_void_p),
+                ("lnf_b", ctypes.c_void_p)]
+
+
+class _Caps(ctypes.Structure):
+    """GPT2Caps (cpu/forward_cpu.h:21-27)."""
+    _fields_ = [("embed", ctypes.c_void_p), ("blocks", ctypes.c_void_p),
+                ("final_ln", ctypes.c_void_p), ("logits", ctypes.c_void_p),
+                ("logits_all", ctypes.c_int)]
+
+
 class RefCPU:
-    """The reference's own attention() (cpu/forward_cpu.c:83-116), compiled from its source."""
+    """The reference's own attention() (cpu/forward_cpu.c:83-116) and whole fp32 forward
+    (gpt2_forward_cpu, cpu/forward_cpu.c:118), compiled from its source."""
 
     def __init__(self, path: str | None = None):
         path = path or os.path.join(REF_DIR, "libref_cpu.so")
@@ -111,7 +135,32 @@ class RefCPU:
         lib = ctypes.CDLL(path)
         lib.ref_cpu_attention.argtypes = [_f32p, _f32p, ctypes.c_int]
         lib.ref_cpu_attention.restype = ctypes.c_int
+        lib.gpt2_forward_cpu.argtypes = [ctypes.POINTER(_Weights), ctypes.c_void_p, ctypes.c_int,
+                                         ctypes.POINTER(_Caps)]
+        lib.gpt2_forward_cpu.restype = None
         self.lib = lib
+
+    def forward_logits(self, tensors: dict, ids) -> np.ndarray:
+        """Logits [T, 50257] of the reference's fp32 forward over ids. tensors maps the names
+        'wte', 'wpe', 'h{L}.{name}', 'lnf_g', 'lnf_b' to fp32 arrays of the reference's shapes."""
+        keep = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in tensors.items()}
+        w = _Weights()
+        w.data = None
+        w.n_floats = 0
+        w.wte = keep["wte"].ctypes.data
+        w.wpe = keep["wpe"].ctypes.data
+        for L in range(12):
+            for n in _LAYER_NAMES:
+                setattr(w.layers[L], n, keep[f"h{L}.{n}"].ctypes.data)
+        w.lnf_g = keep["lnf_g"].ctypes.data
+        w.lnf_b = keep["lnf_b"].ctypes.data
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        logits = np.zeros((len(ids), keep["wte"].shape[0]), dtype=np.float32)
+        caps = _Caps()
+        caps.logits = logits.ctypes.data
+        caps.logits_all = 1
+        self.lib.gpt2_forward_cpu(ctypes.byref(w), ids.ctypes.data, len(ids), ctypes.byref(caps))
+        return logits
 
     def prefill(self, qkv: np.ndarray) -> np.ndarray:
         qkv = np.ascontiguousarray(qkv, dtype=np.float32)
@@ -137,6 +186,7 @@ class RefGPU:
             "ref_gpu_attn_decode": [vp, vp, vp, ci, ci, ci],
             "ref_gpu_kv_append_one": [vp, ci, ci, vp, ci],
             "ref_gpu_kv_scatter_prefill": [vp, ci, ci, vp, ci],
+            "ref_gpu_decode_step": [vp, vp, ci, ci, ci, vp, vp],
         }.items():
             fn = getattr(lib, name)
             fn.argtypes = args
@@ -165,6 +215,13 @@ class RefGPU:
                            t: int) -> None:
         self._ok(self.lib.ref_gpu_kv_scatter_prefill(kv_ptr, max_t, layer, qkv_ptr, t),
                  "ref scatter")
+
+
+    def decode_step(self, weights_ptr: int, kv_ptr: int, max_t: int, token: int, pos: int,
+                    logits_ptr: int | None, caps_ptr: int | None = None) -> None:
+        """The reference's gpt2_decode_step_cuda for one sequence (GEMV backend, fp16 path)."""
+        self._ok(self.lib.ref_gpu_decode_step(weights_ptr, kv_ptr, max_t, token, pos, logits_ptr,
+                                              caps_ptr), "ref decode step")
 
 
 def seeded_qkv(seed: int, t: int, cols: int = QKV) -> np.ndarray:

@@ -6,7 +6,9 @@
  * builds it into oracle/_ref/libref_cpu.so with the reference's own flag set (gcc -O2 -fopenmp).
  *
  * Used by tests (to pin oracle/attn_oracle.c and to make tests/golden/) and by bench.py's reference
- * arm / cpu_baseline, which time this exact code on the host cores.
+ * arm / cpu_baseline, which time this exact code on the host cores. The include also exports the
+ * reference's whole fp32 forward, gpt2_forward_cpu (cpu/forward_cpu.c:118), unchanged: the decode
+ * step tests use it as the CPU oracle of the model around the attention.
  */
 #include "forward_cpu.c"
 

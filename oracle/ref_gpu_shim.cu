@@ -11,6 +11,8 @@
 //   gpt2_attn_decode           cuda/kvcache.cu:207-210
 //   gpt2_kv_append_one         cuda/kvcache.cu:204-206
 //   gpt2_kv_scatter_prefill    cuda/kvcache.cu:78-81
+//   gpt2_decode_step_cuda      cuda/kvcache.cu:233-269 with GPT2_BACKEND_GEMV (kvcache.cu:280-290),
+//                              the reference's fp16 decode path (M=1 GEMVs + its attention)
 #include "kernels.cuh"
 #include "kvcache.cuh"
 #include <cuda_runtime.h>
@@ -53,6 +55,25 @@ int ref_gpu_kv_append_one(void *kv_data, int maxT, int L, const void *qkv, int p
 int ref_gpu_kv_scatter_prefill(void *kv_data, int maxT, int L, const void *qkv, int T) {
     GPT2KVCache kv = view(kv_data, maxT);
     gpt2_kv_scatter_prefill(&kv, L, (const half *)qkv, T);
+    return (int)cudaDeviceSynchronize();
+}
+
+// One decode step of ONE sequence through the reference's own step function. weights points at a
+// GPT2WeightsGPU (cuda/kernels.cuh:41-48) whose fp16 tensors the caller owns (q must be NULL);
+// kv_data is that sequence's [L][K|V][H][maxT][D] arena, holding positions 0..pos-1. logits [V]
+// may be NULL; caps (14 x 768 halves) may be NULL.
+int ref_gpu_decode_step(const void *weights, void *kv_data, int maxT, int token, int pos, void *logits,
+                        void *caps) {
+    static GPT2ScratchGPU s;
+    static bool have = false;
+    if (!have) {
+        gpt2_scratch_alloc(&s, 1);
+        have = true;
+    }
+    GPT2KVCache kv = view(kv_data, maxT);
+    kv.len = pos;
+    gpt2_decode_step_cuda(&GPT2_BACKEND_GEMV, static_cast<const GPT2WeightsGPU *>(weights), &kv,
+                          token, pos, &s, static_cast<half *>(logits), static_cast<half *>(caps));
     return (int)cudaDeviceSynchronize();
 }
 
