@@ -8,8 +8,10 @@ kernel (gpt2_attention_b200_batched). FLOPs per layer = 4*P^2*64*12/2 = 2*P^2*76
 
 The same JSON line also carries configs[2] (decode attention, M=1 per layer, 12 layers in one CUDA
 graph, ctx 1023: KV-read GB/s), configs[3]'s per-GPU share (batched prefill B=64 x P=1024 x 12
-layers), the end-to-end number through the C ABI with host buffers, the roofline of the dominant
-kernel, the reference CPU baseline and the SM clocks sampled during the timed region.
+layers), configs[4] (GPT-2-124M greedy decode of 64 prompts to ctx 1023 around the attention:
+tok/s and the attention share of the step, top-level key decode_tok_per_s), the end-to-end number
+through the C ABI with host buffers, the roofline of the dominant kernel, the reference CPU baseline
+and the SM clocks sampled during the timed region.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs the same per-GPU workload on its own
 sequences (weak scaling, no collective on the data path); the only collectives are a barrier and a
@@ -19,6 +21,7 @@ MAX all-reduce of the timings. `--impl reference` times the reference's own CPU 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -381,6 +384,81 @@ def bench_batched(torch, lib, steps, warmup, world, rank, seed):
             "aggregate_tflops": total_flops / (ms * 1e-3) / 1e12}
 
 
+def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023):
+    """GPT-2-124M greedy decode of 64 prompts (lengths U[1,512], ids U[0,50257)) to a
+    context of 1023 tokens, sequences sharded across ranks. Random-init weights (N(0, 0.02), the
+    tied fp16 head), caches in the reference layout. Every sequence advances one position per step:
+    a prompt token is consumed while the prompt lasts, the argmax is appended after it (lock-step
+    generation, one CUDA graph replay per step). Timed on the device from the upload of the prompts
+    to the download of every token (both from/to pinned host memory)."""
+    rng = np.random.default_rng(seed)
+    plen_all = rng.integers(1, 513, size=total_seqs).astype(np.int32)
+    prompt_all = rng.integers(0, G.VOCAB, size=(total_seqs, 512)).astype(np.int32)
+    lo, hi = shard_range(total_seqs, rank, world)
+    B = hi - lo
+    n_steps = ctx
+    weights = G.ModelWeights(torch, "cuda", seed=seed, hf_init=True)
+    arena = torch.zeros(B, G.N_LAYER, 2, G.N_HEAD, G.N_CTX, 64, dtype=torch.float16, device="cuda")
+    kvs = (G.GPT2KVCache * B)()
+    for b in range(B):
+        kvs[b] = G.cache_view(arena[b].data_ptr(), G.N_LAYER, G.N_CTX)
+    h = ctypes.c_void_p()
+    lib.check(lib.gpt2_b200_batch_create(ctypes.byref(h), ctypes.byref(weights.struct), kvs, B),
+              "gpt2_b200_batch_create")
+    h_prompt = torch.from_numpy(prompt_all[lo:hi].copy()).pin_memory()
+    h_plen = torch.from_numpy(plen_all[lo:hi].copy()).pin_memory()
+    h_out = torch.empty((B, n_steps + 1), dtype=torch.int32).pin_memory()
+    d_prompt = torch.empty((B, 512), dtype=torch.int32, device="cuda")
+    d_plen = torch.empty(B, dtype=torch.int32, device="cuda")
+    d_out = torch.empty((B, n_steps + 1), dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def run(flags):
+        d_prompt.copy_(h_prompt, non_blocking=True)
+        d_plen.copy_(h_plen, non_blocking=True)
+        lib.check(lib.gpt2_b200_batch_generate(h, d_prompt.data_ptr(), 512, d_plen.data_ptr(), n_steps,
+                                               d_out.data_ptr(), n_steps + 1, flags, stream.cuda_stream),
+                  "gpt2_b200_batch_generate")
+        h_out.copy_(d_out, non_blocking=True)
+
+    def timed(flags):
+        run(flags)  # warm-up (the first call also captures the step's graph)
+        torch.cuda.synchronize()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(int(20e6))  # hold the stream while the host queues the steps
+        s.record(stream)
+        run(flags)
+        e.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(s.elapsed_time(e), world)
+
+    ms = timed(0)
+    tokens = h_out.numpy().copy()
+    ms_attn = timed(G.GEN_ATTENTION_ONLY)
+    launches = lib.gpt2_b200_batch_launches_per_step(h, 0)
+    lib.gpt2_b200_batch_destroy(h)
+    status = lib.status()
+    plen = plen_all[lo:hi]
+    prompts_kept = all(np.array_equal(tokens[b, :plen[b]], prompt_all[lo + b, :plen[b]])
+                       for b in range(B))
+    # Tokens the model produced (all ranks): the step at position t emits the token of t+1, which is
+    # generated once t+1 >= the prompt length.
+    generated = int((n_steps + 1 - plen_all).clip(min=0).sum())
+    # HBM bytes the run must move on this rank: every weight once per step (linear layers and the
+    # tied head) and each sequence's K/V of all layers over its context at every step.
+    w_bytes = 2.0 * (G.N_LAYER * (G.QKV_DIM * G.N_EMBD + G.N_EMBD * G.N_EMBD + 2 * G.FFN * G.N_EMBD)
+                     + G.VOCAB * G.N_EMBD)
+    kv_bytes = sum(B * decode_bytes(t + 1) for t in range(n_steps))
+    return {"tok_per_s": generated / (ms * 1e-3), "processed_tok_per_s": total_seqs * n_steps / (ms * 1e-3),
+            "ms_total": ms, "us_per_step": ms * 1e3 / n_steps, "steps": n_steps,
+            "sequences_per_rank": B, "generated_tokens": generated,
+            "attention_share": ms_attn / ms, "attention_us_per_step": ms_attn * 1e3 / n_steps,
+            "hbm_gbs_per_gpu": (n_steps * w_bytes + kv_bytes) / (ms * 1e-3) / 1e9,
+            "prompts_kept": bool(prompts_kept), "status": status, "launches_per_step": launches,
+            "h2d_bytes": int(h_prompt.numel() * 4 + h_plen.numel() * 4), "d2h_bytes": int(h_out.numel() * 4)}
+
+
 # ---------------------------------------------------------------------------------------- CPU legs
 def cpu_reference_sample(seconds: float, max_layers: int | None = None):
     """Times the reference's own attention() (oracle/_ref, OpenMP over all host threads) on P=1024
@@ -516,6 +594,12 @@ def main(argv=None):
                 sec[f"decode_ctx{c}"] = {k: d[k] for k in ("us_per_step", "kv_gbs", "host_kept_ahead")}
             sec["prefill_per_layer_launches"] = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
             sec["batched_B64"] = bench_batched(torch, lib, 3, args.warmup, world, rank, seed=1200 + rank)
+            md = bench_model_decode(torch, lib, G, world, rank, seed=4242)
+            md["roofline"] = {"bound": "hbm", "achieved": md["hbm_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
+                              "unit": "GB/s", "frac": md["hbm_gbs_per_gpu"] / peaks["hbm_gbs"],
+                              "bytes": "weights once per step + every sequence's K/V over its context"}
+            sec["model_decode_B64"] = md
+            line["decode_tok_per_s"] = md["tok_per_s"]
             e2e = bench_e2e_prefill(torch, lib, min(args.steps, 30), args.warmup, seed=1300 + rank)
             e2e_ms = max_over_ranks(e2e["ms_per_step"], world)
             line["e2e"] = {"value": world * flops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
