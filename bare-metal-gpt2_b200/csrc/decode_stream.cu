@@ -28,16 +28,8 @@ namespace b200 {
 namespace dstream {
 
 constexpr int HD = 64;
-constexpr int NCW = 16;                      // consumer warps
-constexpr int NT = 32 * (NCW + 1);           // + one producer warp
-constexpr int KPS = 8 * NCW;                 // keys per stage: 8 per consumer warp
 constexpr int NSTAGE = 4;
 constexpr int ROW_BYTES = HD * 2;            // 128 B per key row
-constexpr int STAGE_BYTES = KPS * ROW_BYTES; // 16 KB of K (and 16 KB of V)
-constexpr int OFF_K = 0;
-constexpr int OFF_V = OFF_K + NSTAGE * STAGE_BYTES;
-constexpr int OFF_RED = OFF_V + NSTAGE * STAGE_BYTES;           // [NCW][64] o + [NCW] m + [NCW] l
-constexpr int OFF_BAR = OFF_RED + (NCW * HD + 2 * NCW) * 4;
 constexpr int PART_STRIDE = HD + 2;
 
 struct __align__(8) Bars {
@@ -46,9 +38,27 @@ struct __align__(8) Bars {
     int abort;
     int is_last;
 };
-static_assert(OFF_BAR % 8 == 0, "mbarriers need 8-byte alignment");
-constexpr int SMEM_BYTES = OFF_BAR + static_cast<int>(sizeof(Bars));
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+
+// Shape of a CTA with NCW consumer warps (plus one producer warp): 8 keys per consumer warp per
+// stage, so KPS = 8 * NCW keys and KPS * 128 bytes each of K and V per stage.
+//   NCW = 16: 128-key stages, 128 KB ring, one CTA per SM (few (job, head) pairs: the GPT-2
+//             12-layer step of one sequence, split over the context when pairs are fewer than SMs);
+//   NCW = 4:  32-key stages, 32 KB ring, six CTAs per SM (many pairs: a batch of sequences; the
+//             per-CTA ramp and tail of one pair overlap the others' streaming).
+template <int NCW>
+struct Cfg {
+    static constexpr int NT = 32 * (NCW + 1);
+    static constexpr int KPS = 8 * NCW;
+    static constexpr int STAGE_BYTES = KPS * ROW_BYTES;
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = OFF_K + NSTAGE * STAGE_BYTES;
+    static constexpr int OFF_RED = OFF_V + NSTAGE * STAGE_BYTES;  // [NCW][64] o, [NCW] m, [NCW] l
+    static constexpr int OFF_BAR = OFF_RED + (NCW * HD + 2 * NCW) * 4;
+    static constexpr int SMEM_BYTES = OFF_BAR + static_cast<int>(sizeof(Bars));
+    static_assert(OFF_BAR % 8 == 0, "mbarriers need 8-byte alignment");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+constexpr int NCW_FEW = 16, NCW_MANY = 4;
 
 struct Params {
     const __half *q;
@@ -78,7 +88,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsign
     return __all_sync(0xffffffffu, ok);
 }
 
-__global__ void __launch_bounds__(NT) k_decode_stream(const Params p) {
+template <int NCW>
+__global__ void __launch_bounds__(32 * (NCW + 1)) k_decode_stream(const Params p) {
+    using C = Cfg<NCW>;
+    constexpr int KPS = C::KPS, STAGE_BYTES = C::STAGE_BYTES;
+    constexpr int OFF_K = C::OFF_K, OFF_V = C::OFF_V, OFF_RED = C::OFF_RED, OFF_BAR = C::OFF_BAR;
     extern __shared__ __align__(128) uint8_t smem[];
     Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
     float *red_o = reinterpret_cast<float *>(smem + OFF_RED);
@@ -328,7 +342,8 @@ int decode_stream_splits(int max_len, long long pairs, int num_sms) {
     const int sms = num_sms > 0 ? num_sms : 148;
     long long n = (sms + pairs / 2) / pairs;  // round(sms / pairs)
     if (n < 1) n = 1;
-    const long long max_n = (max_len + dstream::KPS - 1) / dstream::KPS;
+    const long long max_n = (max_len + dstream::Cfg<dstream::NCW_FEW>::KPS - 1) /
+                            dstream::Cfg<dstream::NCW_FEW>::KPS;
     if (n > max_n) n = max_n;
     return static_cast<int>(n);
 }
@@ -339,8 +354,12 @@ int prepare_decode_stream() {
     DeviceContext *ctx = device_context();
     if (!ctx) return GPT2_B200_ECUDA;
     if (!ctx->decode_attr_done) {
-        if (cudaFuncSetAttribute(dstream::k_decode_stream, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 dstream::SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_FEW>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 dstream::Cfg<dstream::NCW_FEW>::SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_MANY>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 dstream::Cfg<dstream::NCW_MANY>::SMEM_BYTES) != cudaSuccess)
             return GPT2_B200_ECUDA;
         ctx->decode_attr_done = true;
     }
@@ -388,16 +407,20 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.nsplit, H, njobs);
-    cfg.blockDim = dim3(dstream::NT, 1, 1);
-    cfg.dynamicSmemBytes = dstream::SMEM_BYTES;
+    // Many (job, head) pairs, each whole in one CTA: the small CTA shape, several per SM.
+    const bool many = p.nsplit == 1 && static_cast<long long>(njobs) * H >= 2LL * ctx->num_sms;
+    cfg.blockDim = dim3(many ? dstream::Cfg<dstream::NCW_MANY>::NT : dstream::Cfg<dstream::NCW_FEW>::NT, 1, 1);
+    cfg.dynamicSmemBytes = many ? dstream::Cfg<dstream::NCW_MANY>::SMEM_BYTES
+                                : dstream::Cfg<dstream::NCW_FEW>::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, dstream::k_decode_stream, p) == cudaSuccess ? GPT2_B200_OK
-                                                                                 : GPT2_B200_ECUDA;
+    const cudaError_t err = many ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY>, p)
+                                 : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW>, p);
+    return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 
 }  // namespace b200

@@ -111,6 +111,35 @@ def test_decode_batched_sequences(cuda, lib, oracle, cache):
         assert_close(got[b], want, f"seq {b} (layer {L}, len {n})")
 
 
+def test_decode_batched_many_sequences(cuda, lib, oracle, cache):
+    """Enough (sequence, head) pairs for the small-CTA shape (several CTAs per SM, each pair whole in
+    one CTA): 40 sequences x 12 heads, lengths covering stage edges of 32 keys and the full cache."""
+    torch = cuda
+    rng = np.random.default_rng(77)
+    lens = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1023, 1024] + \
+        [int(x) for x in rng.integers(1, MAXT + 1, size=27)]
+    B = len(lens)
+    slab = O.H * MAXT * O.D
+    base = cache["d_arena"].data_ptr()
+    layers = [b % L_ for b in range(B)]
+    kptr = torch.tensor([base + (2 * L) * slab * 2 for L in layers], dtype=torch.int64, device="cuda")
+    vptr = torch.tensor([base + (2 * L + 1) * slab * 2 for L in layers], dtype=torch.int64, device="cuda")
+    d_lens = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.from_numpy(np.random.default_rng(78).standard_normal((B, O.QKV), dtype=np.float32)
+                         .astype(np.float16)).cuda()
+    att = torch.empty((B, O.E), dtype=torch.float16, device="cuda")
+    rc = lib.gpt2_attn_decode_b200_batched(att.data_ptr(), O.E, q.data_ptr(), O.QKV, kptr.data_ptr(),
+                                           vptr.data_ptr(), d_lens.data_ptr(), B, O.H, MAXT, 0, None)
+    lib.check(rc, "batched decode")
+    torch.cuda.synchronize()
+    got = host(att)
+    qf = host(q)
+    for b, (L, n) in enumerate(zip(layers, lens)):
+        want = oracle.decode(qf[b, :O.E], cache["arena"][L, 0], cache["arena"][L, 1], n)
+        assert_close(got[b], want, f"seq {b} (layer {L}, len {n})")
+    assert lib.status() == 0
+
+
 def test_device_length_out_of_range_reports_status(cuda, lib, cache):
     torch = cuda
     att = torch.full((L_, O.E), 7.0, dtype=torch.float16, device="cuda")
