@@ -500,18 +500,53 @@ unsigned long long *g_keys[64] = {};
 size_t g_keys_n[64] = {};
 }  // namespace
 
+namespace {
+// Recently used plans of gpt2_b200_linear (a plan encodes two tensor maps and picks the split,
+// which costs host time a per-token GEMV slot should not pay every call).
+struct LinearCacheEntry {
+    const void *C, *A, *W, *bias;
+    long long ldc, lda;
+    int B, N, K, epi, device;
+    bool valid;
+    lin::Plan plan;
+};
+constexpr int kLinearCache = 16;
+thread_local LinearCacheEntry t_lin[kLinearCache];
+thread_local int t_lin_next = 0;
+}  // namespace
+
 int gpt2_b200_linear(gpt2_half *C, long long ldc, const gpt2_half *A, long long lda,
                      const gpt2_half *W, const gpt2_half *bias, int B, int N, int K, int epi,
                      cudaStream_t stream) {
     if (epi < GPT2_B200_LINEAR_STORE || epi > GPT2_B200_LINEAR_RESID || !C || ldc < N)
         return GPT2_B200_EINVAL;
-    lin::Plan pl;
-    const int e = epi == GPT2_B200_LINEAR_STORE ? lin::EPI_STORE
-                  : epi == GPT2_B200_LINEAR_GELU ? lin::EPI_GELU
-                                                 : lin::EPI_RESID;
-    int rc = lin::plan_linear(&pl, e, W, N, K, A, lda, B, bias, C, ldc, 0, 0);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GPT2_B200_ECUDA;
+    for (const LinearCacheEntry &e : t_lin)
+        if (e.valid && e.C == C && e.A == A && e.W == W && e.bias == bias && e.ldc == ldc &&
+            e.lda == lda && e.B == B && e.N == N && e.K == K && e.epi == epi && e.device == dev)
+            return lin::launch_linear(e.plan, stream);
+    const int ep = epi == GPT2_B200_LINEAR_STORE ? lin::EPI_STORE
+                   : epi == GPT2_B200_LINEAR_GELU ? lin::EPI_GELU
+                                                  : lin::EPI_RESID;
+    LinearCacheEntry &e = t_lin[t_lin_next];
+    e.valid = false;
+    int rc = lin::plan_linear(&e.plan, ep, W, N, K, A, lda, B, bias, C, ldc, 0, 0);
     if (rc != GPT2_B200_OK) return rc;
-    return lin::launch_linear(pl, stream);
+    e.C = C;
+    e.A = A;
+    e.W = W;
+    e.bias = bias;
+    e.ldc = ldc;
+    e.lda = lda;
+    e.B = B;
+    e.N = N;
+    e.K = K;
+    e.epi = epi;
+    e.device = dev;
+    e.valid = true;
+    t_lin_next = (t_lin_next + 1) % kLinearCache;
+    return lin::launch_linear(e.plan, stream);
 }
 
 int gpt2_b200_linear_argmax(gpt2_half *logits, long long ldl, const gpt2_half *A, long long lda,

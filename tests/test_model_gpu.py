@@ -64,6 +64,27 @@ def test_linear_matches_fp64(cuda, lib, B, N, K, epi):
     assert lib.status() == 0
 
 
+@pytest.mark.parametrize("N,K", [(2304, 768), (768, 3072), (V, 768)])
+def test_gemv_slot_matches_fp64(cuda, lib, N, K):
+    """gpt2_gemv_b200 in the GPT2Backend.gemv slot's form: C[1,N] = A[1,K] W^T + bias (and
+    bias NULL, as the reference's head call passes), repeated (cached plan) with new inputs."""
+    torch = cuda
+    g = _gen(torch, 500 + N + K)
+    W = (0.05 * torch.randn(N, K, generator=g, device="cuda")).half()
+    bias = (0.1 * torch.randn(N, generator=g, device="cuda")).half()
+    A = torch.empty(1, K, dtype=torch.float16, device="cuda")
+    C = torch.empty(1, N, dtype=torch.float16, device="cuda")
+    for rep, b in enumerate((bias, None, bias)):
+        A.copy_(torch.randn(1, K, generator=g, device="cuda").half())
+        lib.gpt2_gemv_b200(C.data_ptr(), A.data_ptr(), W.data_ptr(),
+                           b.data_ptr() if b is not None else None, N, K)
+        assert lib.gpt2_b200_last_error() == G.OK
+        torch.cuda.synchronize()
+        want = A.double() @ W.double().T + (b.double() if b is not None else 0.0)
+        want = want.half().double()
+        ulp_check(C, want, want.abs(), f"gemv N={N} K={K} rep {rep}")
+
+
 @pytest.mark.parametrize("B", [1, 3, 64])
 def test_linear_argmax_matches_fp64_and_first_index_on_ties(cuda, lib, B):
     torch = cuda
