@@ -62,6 +62,11 @@ def parse_args(argv=None):
     ap.add_argument("--no-secondary", action="store_true",
                     help="headline only (decode / batched / e2e / cpu legs skipped)")
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
+    ap.add_argument("--legs", default="all",
+                    help="comma list of secondary legs to run: decode, decode_b64, per_layer, batched, "
+                         "model_decode, e2e, cpu (default all; for profiling one leg)")
+    ap.add_argument("--model-steps", type=int, default=1023,
+                    help="decode steps of the configs[4] leg (1023 = the configs' ctx; fewer only to profile)")
     return ap.parse_args(argv)
 
 
@@ -311,6 +316,44 @@ def bench_decode(torch, lib, G, steps, warmup, ctx, seed):
     us = region / steps * 1e3
     return {"ctx": ctx, "us_per_step": us, "kv_gbs": nbytes / (us * 1e-6) / 1e9,
             "bytes_per_step": nbytes, "rotating_caches": rot, "host_kept_ahead": ahead}
+
+
+def bench_decode_batched(torch, lib, steps, warmup, world, rank, ctx, seed, total_seqs=64):
+    """Decode attention of one 12-layer step for a batch of sequences (configs[4]'s attention): this
+    rank's share of 64 sequences, each with its own [12][K|V][12][1024][64] cache at context ctx;
+    one batched launch per layer (all sequences x 12 heads). The read set (64 x 37.7 MB at ctx 1023)
+    is far above L2."""
+    lo, hi = shard_range(total_seqs, rank, world)
+    B = hi - lo
+    arena = seeded_fp16(torch, (B, LAYERS, 2, H, MAXT, D), seed, "cuda")
+    q = seeded_fp16(torch, (LAYERS, B, QKV), seed + 1, "cuda")
+    att = torch.empty((LAYERS, B, E), dtype=torch.float16, device="cuda")
+    slab = H * MAXT * D * 2
+    kp = torch.tensor([[arena[b].data_ptr() + 2 * L * slab for b in range(B)] for L in range(LAYERS)],
+                      dtype=torch.int64, device="cuda")
+    vp = torch.tensor([[arena[b].data_ptr() + (2 * L + 1) * slab for b in range(B)]
+                       for L in range(LAYERS)], dtype=torch.int64, device="cuda")
+    lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        for L in range(LAYERS):
+            rc = lib.gpt2_attn_decode_b200_batched(att[L].data_ptr(), E, q[L].data_ptr(), QKV,
+                                                   kp[L].data_ptr(), vp[L].data_ptr(), lens.data_ptr(),
+                                                   B, H, MAXT, MAXT, stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError("batched decode launch failed")
+    host_s = host_seconds_per_step(torch, step, warmup)
+    barrier(world)
+    region, ahead = timed_region(torch, stream, steps, step, host_s)
+    ms = max_over_ranks(region / steps, world)
+    st = lib.gpt2_b200_status(1)
+    if st:
+        raise RuntimeError(f"device status 0x{st:x} after batched decode bench")
+    nbytes = B * decode_bytes(ctx)
+    return {"ctx": ctx, "sequences_per_rank": B, "us_per_step": ms * 1e3,
+            "kv_gbs_per_gpu": nbytes / (ms * 1e-3) / 1e9, "launches_per_step": LAYERS,
+            "host_kept_ahead": ahead}
 
 
 def bench_e2e_prefill(torch, lib, steps, warmup, seed, nstreams=3):
@@ -580,38 +623,52 @@ def main(argv=None):
         "clocks": clocks.summary(),
     }
 
+    legs = set(args.legs.split(",")) if args.legs != "all" else {
+        "decode", "decode_b64", "per_layer", "batched", "model_decode", "e2e", "cpu"}
     if not args.no_secondary:
         sec = {}
         try:
-            dec = bench_decode(torch, lib, G, min(args.steps, 400), args.warmup, CTX, seed=500 + rank)
-            dec["roofline"] = {"bound": "hbm", "achieved": dec["kv_gbs"], "peak": peaks["hbm_gbs"],
-                               "unit": "GB/s", "frac": dec["kv_gbs"] / peaks["hbm_gbs"],
-                               "traffic": profile_traffic("decode_stream_ctx1023_L12"),
-                               "kernel": "k_decode_stream"}
-            sec["decode_ctx1023"] = dec
-            for c in (128, 512):
-                d = bench_decode(torch, lib, G, min(args.steps, 200), args.warmup, c, seed=700 + rank)
-                sec[f"decode_ctx{c}"] = {k: d[k] for k in ("us_per_step", "kv_gbs", "host_kept_ahead")}
-            sec["prefill_per_layer_launches"] = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
-            sec["batched_B64"] = bench_batched(torch, lib, 3, args.warmup, world, rank, seed=1200 + rank)
-            md = bench_model_decode(torch, lib, G, world, rank, seed=4242)
-            md["roofline"] = {"bound": "hbm", "achieved": md["hbm_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
-                              "unit": "GB/s", "frac": md["hbm_gbs_per_gpu"] / peaks["hbm_gbs"],
-                              "bytes": "weights once per step + every sequence's K/V over its context"}
-            sec["model_decode_B64"] = md
-            line["decode_tok_per_s"] = md["tok_per_s"]
-            e2e = bench_e2e_prefill(torch, lib, min(args.steps, 30), args.warmup, seed=1300 + rank)
-            e2e_ms = max_over_ranks(e2e["ms_per_step"], world)
-            line["e2e"] = {"value": world * flops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                           "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                           "ms_per_step": e2e_ms, "host_kept_ahead": e2e["host_kept_ahead"],
-                           "path": "per layer: pinned host qkv -> cudaMemcpyAsync -> gpt2_attention_b200_stream "
-                                   f"(the reference's attention slot) -> att to pinned host, {e2e['streams']} "
-                                   "streams overlapping upload, attention and download"}
+            if "decode" in legs:
+                dec = bench_decode(torch, lib, G, min(args.steps, 400), args.warmup, CTX, seed=500 + rank)
+                dec["roofline"] = {"bound": "hbm", "achieved": dec["kv_gbs"], "peak": peaks["hbm_gbs"],
+                                   "unit": "GB/s", "frac": dec["kv_gbs"] / peaks["hbm_gbs"],
+                                   "traffic": profile_traffic("decode_stream_ctx1023_L12"),
+                                   "kernel": "k_decode_stream"}
+                sec["decode_ctx1023"] = dec
+                for c in (128, 512):
+                    d = bench_decode(torch, lib, G, min(args.steps, 200), args.warmup, c, seed=700 + rank)
+                    sec[f"decode_ctx{c}"] = {k: d[k] for k in ("us_per_step", "kv_gbs", "host_kept_ahead")}
+            if "decode_b64" in legs:
+                for c in (512, 1023):
+                    d = bench_decode_batched(torch, lib, 20, args.warmup, world, rank, c, seed=800 + rank)
+                    d["roofline"] = {"bound": "hbm", "achieved": d["kv_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
+                                     "unit": "GB/s", "frac": d["kv_gbs_per_gpu"] / peaks["hbm_gbs"],
+                                     "kernel": "k_decode_stream<4>"}
+                    sec[f"decode_B64_ctx{c}"] = d
+            if "per_layer" in legs:
+                sec["prefill_per_layer_launches"] = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
+            if "batched" in legs:
+                sec["batched_B64"] = bench_batched(torch, lib, 3, args.warmup, world, rank, seed=1200 + rank)
+            if "model_decode" in legs:
+                md = bench_model_decode(torch, lib, G, world, rank, seed=4242, ctx=args.model_steps)
+                md["roofline"] = {"bound": "hbm", "achieved": md["hbm_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
+                                  "unit": "GB/s", "frac": md["hbm_gbs_per_gpu"] / peaks["hbm_gbs"],
+                                  "bytes": "weights once per step + every sequence's K/V over its context"}
+                sec["model_decode_B64"] = md
+                line["decode_tok_per_s"] = md["tok_per_s"]
+            if "e2e" in legs:
+                e2e = bench_e2e_prefill(torch, lib, min(args.steps, 30), args.warmup, seed=1300 + rank)
+                e2e_ms = max_over_ranks(e2e["ms_per_step"], world)
+                line["e2e"] = {"value": world * flops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                               "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                               "ms_per_step": e2e_ms, "host_kept_ahead": e2e["host_kept_ahead"],
+                               "path": "per layer: pinned host qkv -> cudaMemcpyAsync -> gpt2_attention_b200_stream "
+                                       f"(the reference's attention slot) -> att to pinned host, {e2e['streams']} "
+                                       "streams overlapping upload, attention and download"}
         except Exception as ex:  # noqa: BLE001 - the headline stands; the failure is reported
             sec["error"] = repr(ex)
         line["secondary"] = sec
-        if rank == 0 and world == 1:
+        if rank == 0 and world == 1 and "cpu" in legs:
             cpu = cpu_reference_sample(args.cpu_sample_seconds)
             line["cpu_baseline"] = {"value": cpu["tflops"], "unit": "TFLOP/s", "cores": cpu["threads"],
                                     "kind": cpu["kind"],
