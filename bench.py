@@ -566,14 +566,32 @@ def run_reference(args, rank, world):
                              "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
 # ---------------------------------------------------------------------------------------- main
+def emit(line) -> None:
+    """Writes the one JSON line to the process's real standard output (see main)."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+_JSON_OUT = None
+
+
 def main(argv=None):
+    global _JSON_OUT
     args = parse_args(argv)
     rank, world, local = dist_env()
+    # Standard output carries exactly one JSON line. Everything else that libraries print to file
+    # descriptor 1 (NCCL's version banner among them) is sent to standard error: fd 1 points at
+    # stderr for the rest of the run and the JSON line goes to a duplicate of the original stdout.
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if args.warmup < 3:
@@ -584,8 +602,6 @@ def main(argv=None):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # stdout carries exactly one JSON line: NCCL's own log (version banner included) goes to stderr
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import gpt2_b200 as G
@@ -676,7 +692,7 @@ def main(argv=None):
                                               f"(median {cpu['per_layer_s'] * 1e3:.1f} ms each), "
                                               "scaled to TFLOP/s"}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
