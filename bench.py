@@ -450,7 +450,11 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
               "gpt2_b200_batch_create")
     h_prompt = torch.from_numpy(prompt_all[lo:hi].copy()).pin_memory()
     h_plen = torch.from_numpy(plen_all[lo:hi].copy()).pin_memory()
-    h_out = torch.empty((B, n_steps + 1), dtype=torch.int32).pin_memory()
+    # Multi-GPU: every rank's tokens are gathered over NVLink into rank 0's memory (NCCL all-gather,
+    # equal shards), then copied to the host once; with one GPU the tokens go straight to the host.
+    gather = world > 1 and total_seqs % world == 0
+    d_all = torch.empty((total_seqs, n_steps + 1), dtype=torch.int32, device="cuda") if gather else None
+    h_out = torch.empty((total_seqs if gather else B, n_steps + 1), dtype=torch.int32).pin_memory()
     d_prompt = torch.empty((B, 512), dtype=torch.int32, device="cuda")
     d_plen = torch.empty(B, dtype=torch.int32, device="cuda")
     d_out = torch.empty((B, n_steps + 1), dtype=torch.int32, device="cuda")
@@ -462,7 +466,13 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
         lib.check(lib.gpt2_b200_batch_generate(h, d_prompt.data_ptr(), 512, d_plen.data_ptr(), n_steps,
                                                d_out.data_ptr(), n_steps + 1, flags, stream.cuda_stream),
                   "gpt2_b200_batch_generate")
-        h_out.copy_(d_out, non_blocking=True)
+        if gather:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(d_all, d_out)
+            if rank == 0:
+                h_out.copy_(d_all, non_blocking=True)
+        else:
+            h_out.copy_(d_out, non_blocking=True)
 
     def timed(flags):
         run(flags)  # warm-up (the first call also captures the step's graph)
@@ -482,9 +492,12 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
     launches = lib.gpt2_b200_batch_launches_per_step(h, 0)
     lib.gpt2_b200_batch_destroy(h)
     status = lib.status()
-    plen = plen_all[lo:hi]
-    prompts_kept = all(np.array_equal(tokens[b, :plen[b]], prompt_all[lo + b, :plen[b]])
-                       for b in range(B))
+    if gather:  # rank 0 holds every sequence's tokens
+        rows, first = (range(total_seqs), 0) if rank == 0 else (range(0), 0)
+    else:
+        rows, first = range(B), lo
+    prompts_kept = all(np.array_equal(tokens[r, :plen_all[first + r]], prompt_all[first + r, :plen_all[first + r]])
+                       for r in rows)
     # Tokens the model produced (all ranks): the step at position t emits the token of t+1, which is
     # generated once t+1 >= the prompt length.
     generated = int((n_steps + 1 - plen_all).clip(min=0).sum())
@@ -499,7 +512,9 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
             "attention_share": ms_attn / ms, "attention_us_per_step": ms_attn * 1e3 / n_steps,
             "hbm_gbs_per_gpu": (n_steps * w_bytes + kv_bytes) / (ms * 1e-3) / 1e9,
             "prompts_kept": bool(prompts_kept), "status": status, "launches_per_step": launches,
-            "h2d_bytes": int(h_prompt.numel() * 4 + h_plen.numel() * 4), "d2h_bytes": int(h_out.numel() * 4)}
+            "h2d_bytes": int(h_prompt.numel() * 4 + h_plen.numel() * 4),
+            "d2h_bytes": int(h_out.numel() * 4) if (rank == 0 or not gather) else 0,
+            "output_gather": "NCCL all-gather over NVLink to rank 0, one D2H" if gather else "D2H per rank"}
 
 
 # ---------------------------------------------------------------------------------------- CPU legs
