@@ -77,6 +77,11 @@ __device__ __forceinline__ void epi_elem(const Params &p, const QkvMeta *meta, i
     }
 }
 
+__device__ __forceinline__ void dsmem_st_v4(uint32_t cluster_saddr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_saddr), "f"(v.x),
+                 "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
 __device__ __forceinline__ float4 dsmem_ld_v4(uint32_t cluster_saddr) {
     float4 v;
     asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -96,13 +101,17 @@ __global__ void __launch_bounds__(NT, 1) k_linear_tc(const __grid_constant__ CUt
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int stage_bytes = W_ATOM_BYTES + p.bpad * 128;
     // The ring; after the last MMA the split-K path reuses it for the partial tile [bpad][128].
-    const int ring = max(p.nstage * stage_bytes, p.cs > 1 ? p.bpad * BM * 4 : 0);
+    // The stage ring; the pull reduction reuses it for the partial tile [bpad][128] after the MMAs.
+    const int ring = max(p.nstage * stage_bytes, (p.cs > 1 && !p.push) ? p.bpad * BM * 4 : 0);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + ring);
     uint64_t *empty = full + MAX_STAGES;
     uint64_t *done = empty + MAX_STAGES;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     unsigned long long *red = reinterpret_cast<unsigned long long *>(smem + ring + 128);
     QkvMeta *meta = reinterpret_cast<QkvMeta *>(smem + ring + 128);
+    // Split K, push reduction: partial columns received from every rank, [rank][128 rows][cpr4] fp32
+    // (own slot too).
+    float *recv = reinterpret_cast<float *>(smem + ring + 128 + p.extra_bytes);
 
     const int rank = static_cast<int>(cluster_rank());
     const int tile = blockIdx.y;
@@ -195,12 +204,14 @@ __global__ void __launch_bounds__(NT, 1) k_linear_tc(const __grid_constant__ CUt
             meta->v[b] = p.v_dst[b];
         }
     }
-    constexpr int XPRE = 16;  // whole-K path: residual inputs of the first 16 columns, prefetched
+    // Residual inputs of this thread's first 16 columns (whole K: columns 0..15; split K: this
+    // rank's columns), prefetched.
+    constexpr int XPRE = 16;
     float xin[XPRE];
 #pragma unroll
     for (int j = 0; j < XPRE; ++j)
-        xin[j] = (EPI == EPI_RESID && p.cs == 1 && n_ok && j < p.B)
-                     ? __half2float(p.out[static_cast<long long>(j) * p.ldo + n])
+        xin[j] = (EPI == EPI_RESID && n_ok && j < my_w && my_lo + j < p.B)
+                     ? __half2float(p.out[static_cast<long long>(my_lo + j) * p.ldo + n])
                      : 0.0f;
     if (EPI == EPI_QKV) __syncthreads();
 
@@ -261,66 +272,132 @@ __global__ void __launch_bounds__(NT, 1) k_linear_tc(const __grid_constant__ CUt
             }
         }
     } else {
-        // Split K: publish this CTA's partial tile in shared memory as [bpad][128] fp32 (column b's
-        // 128 rows at b*128), then rank r reduces its columns [my_lo, my_lo + my_w) over all ranks
-        // in rank order through distributed shared memory (deterministic). Thread t owns rows
-        // 4*(t % 32) .. +3 and the columns my_lo + t/32, +4, ...; two columns per pass, every load
-        // of a pass issued before its first use.
-        float *part = reinterpret_cast<float *>(smem);
-        for (int c = 0; c < p.bpad; c += 16) {
-            uint32_t r[16];
-            tmem_ld16(trow + c, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) part[(c + j) * BM + row] = __uint_as_float(r[j]);
-        }
-        cluster_sync_all();
-        const int q4 = (threadIdx.x & 31) * 4;
-        const int nq = n0 + q4;
-        float bq[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            bq[i] = (p.bias != nullptr && nq + i < p.N) ? __half2float(p.bias[nq + i]) : 0.0f;
-        const uint32_t base = smem_u32(part) + static_cast<uint32_t>(q4 * 4);
-        const int b1 = min(my_lo + my_w, p.B);
-        constexpr int CG = 2;
-        for (int b = my_lo + (threadIdx.x >> 5); b < b1; b += 4 * CG) {
-            float xq[CG][4];
-            float4 t[CG][MAX_CLUSTER];
-#pragma unroll
-            for (int g = 0; g < CG; ++g) {
-                const int bb = b + 4 * g;
-                const bool valid = bb < b1;
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    xq[g][i] = (EPI == EPI_RESID && valid && nq + i < p.N)
-                                   ? __half2float(p.out[static_cast<long long>(bb) * p.ldo + nq + i])
-                                   : 0.0f;
-                const uint32_t off = base + static_cast<uint32_t>(bb * BM * 4);
-#pragma unroll
-                for (int q = 0; q < MAX_CLUSTER; ++q)
-                    t[g][q] = (valid && q < p.cs)
-                                  ? dsmem_ld_v4(dsmem_addr(off, static_cast<uint32_t>(q)))
-                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            }
-#pragma unroll
-            for (int g = 0; g < CG; ++g) {
-                const int bb = b + 4 * g;
-                if (bb >= b1 || !have) continue;
-                float acc[4] = {bq[0], bq[1], bq[2], bq[3]};
-#pragma unroll
-                for (int q = 0; q < MAX_CLUSTER; ++q) {
-                    acc[0] += t[g][q].x;
-                    acc[1] += t[g][q].y;
-                    acc[2] += t[g][q].z;
-                    acc[3] += t[g][q].w;
+        if (p.push) {
+            // Split K: every rank owns the batch columns [r*cpr4, (r+1)*cpr4). Each CTA stores row `row`
+            // of its partial for those columns straight into the owner's receive slot for this rank
+            // (recv[rank][row][..], plain distributed-shared-memory stores; its own columns locally).
+            // One cluster barrier (release / acquire) publishes every store; each owner then sums its
+            // columns over the ranks in rank order (deterministic) from its own shared memory. Nothing
+            // is read remotely, so no CTA has to wait for its peers again before exiting.
+            const uint32_t recv_s = smem_u32(recv);
+            for (int c = 0; c < p.bpad; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(trow + c, r);
+                tmem_wait_ld();
+    #pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const int col = c + 4 * g;
+                    const int q = col / p.cpr4;
+                    const float4 v = make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                                 __uint_as_float(r[4 * g + 2]),
+                                                 __uint_as_float(r[4 * g + 3]));
+                    const uint32_t off =
+                        static_cast<uint32_t>(((rank * BM + row) * p.cpr4 + (col - q * p.cpr4)) * 4);
+                    if (q == rank)
+                        *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(recv) + off) = v;
+                    else
+                        dsmem_st_v4(dsmem_addr(recv_s + off, static_cast<uint32_t>(q)), v);
                 }
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    if (nq + i < p.N) epi_elem<EPI>(p, meta, nq + i, bb, acc[i], xq[g][i]);
             }
+            cluster_sync_all();
+            if (have && n_ok) {
+    #pragma unroll
+                for (int j = 0; j < XPRE; j += 4) {
+                    if (j >= my_w) break;
+                    float a4[4] = {bias_n, bias_n, bias_n, bias_n};
+                    for (int q = 0; q < p.cs; ++q) {
+                        const float4 v = *reinterpret_cast<const float4 *>(recv + (q * BM + row) * p.cpr4 + j);
+                        a4[0] += v.x;
+                        a4[1] += v.y;
+                        a4[2] += v.z;
+                        a4[3] += v.w;
+                    }
+    #pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (my_lo + j + i < p.B) epi_elem<EPI>(p, meta, n, my_lo + j + i, a4[i], xin[j + i]);
+                }
+                for (int j = XPRE; j < my_w; j += 4) {
+                    float a4[4] = {bias_n, bias_n, bias_n, bias_n};
+                    for (int q = 0; q < p.cs; ++q) {
+                        const float4 v = *reinterpret_cast<const float4 *>(recv + (q * BM + row) * p.cpr4 + j);
+                        a4[0] += v.x;
+                        a4[1] += v.y;
+                        a4[2] += v.z;
+                        a4[3] += v.w;
+                    }
+    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int b = my_lo + j + i;
+                        if (b >= p.B) break;
+                        const float x = EPI == EPI_RESID
+                                            ? __half2float(p.out[static_cast<long long>(b) * p.ldo + n])
+                                            : 0.0f;
+                        epi_elem<EPI>(p, meta, n, b, a4[i], x);
+                    }
+                }
+            }
+        } else {
+            // Split K: publish this CTA's partial tile in shared memory as [bpad][128] fp32 (column b's
+            // 128 rows at b*128), then rank r reduces its columns [my_lo, my_lo + my_w) over all ranks
+            // in rank order through distributed shared memory (deterministic). Thread t owns rows
+            // 4*(t % 32) .. +3 and the columns my_lo + t/32, +4, ...; two columns per pass, every load
+            // of a pass issued before its first use.
+            float *part = reinterpret_cast<float *>(smem);
+            for (int c = 0; c < p.bpad; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(trow + c, r);
+                tmem_wait_ld();
+    #pragma unroll
+                for (int j = 0; j < 16; ++j) part[(c + j) * BM + row] = __uint_as_float(r[j]);
+            }
+            cluster_sync_all();
+            const int q4 = (threadIdx.x & 31) * 4;
+            const int nq = n0 + q4;
+            float bq[4];
+    #pragma unroll
+            for (int i = 0; i < 4; ++i)
+                bq[i] = (p.bias != nullptr && nq + i < p.N) ? __half2float(p.bias[nq + i]) : 0.0f;
+            const uint32_t base = smem_u32(part) + static_cast<uint32_t>(q4 * 4);
+            const int b1 = min(my_lo + my_w, p.B);
+            constexpr int CG = 2;
+            for (int b = my_lo + (threadIdx.x >> 5); b < b1; b += 4 * CG) {
+                float xq[CG][4];
+                float4 t[CG][MAX_CLUSTER];
+    #pragma unroll
+                for (int g = 0; g < CG; ++g) {
+                    const int bb = b + 4 * g;
+                    const bool valid = bb < b1;
+    #pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        xq[g][i] = (EPI == EPI_RESID && valid && nq + i < p.N)
+                                       ? __half2float(p.out[static_cast<long long>(bb) * p.ldo + nq + i])
+                                       : 0.0f;
+                    const uint32_t off = base + static_cast<uint32_t>(bb * BM * 4);
+    #pragma unroll
+                    for (int q = 0; q < MAX_CLUSTER; ++q)
+                        t[g][q] = (valid && q < p.cs)
+                                      ? dsmem_ld_v4(dsmem_addr(off, static_cast<uint32_t>(q)))
+                                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+    #pragma unroll
+                for (int g = 0; g < CG; ++g) {
+                    const int bb = b + 4 * g;
+                    if (bb >= b1 || !have) continue;
+                    float acc[4] = {bq[0], bq[1], bq[2], bq[3]};
+    #pragma unroll
+                    for (int q = 0; q < MAX_CLUSTER; ++q) {
+                        acc[0] += t[g][q].x;
+                        acc[1] += t[g][q].y;
+                        acc[2] += t[g][q].z;
+                        acc[3] += t[g][q].w;
+                    }
+    #pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (nq + i < p.N) epi_elem<EPI>(p, meta, nq + i, bb, acc[i], xq[g][i]);
+                }
+            }
+            cluster_sync_all();  // peers may still be reading this CTA's partial tile
         }
-        cluster_sync_all();  // peers may still be reading this CTA's partial tile
     }
 
     tc_fence_before();
@@ -430,12 +507,15 @@ int plan_linear(Plan *pl, int epi, const __half *W, int N, int K, const __half *
     // a cycle), so shared memory is padded to cap the CTAs per SM.
     const size_t limit = 227 * 1024;
     auto size_for = [&](int c, int *nstage) -> size_t {
-        const size_t fixed = 1024 + 128 + p.extra_bytes;
+        const int cpr4 = c > 1 ? ((p.bpad + c - 1) / c + 3) / 4 * 4 : p.bpad;
+        const bool push = c > 1 && p.bpad <= PUSH_MAX_BPAD;
+        const size_t recv = push ? static_cast<size_t>(c) * BM * cpr4 * 4 : 0;
+        const size_t fixed = 1024 + 128 + p.extra_bytes + recv;
         int ns = std::min(MAX_STAGES, (p.atoms + c - 1) / c);
         while (ns > 1 && fixed + static_cast<size_t>(ns) * stage_bytes > limit) --ns;
         *nstage = ns;
         const size_t ring = std::max(static_cast<size_t>(ns) * stage_bytes,
-                                     c > 1 ? static_cast<size_t>(p.bpad) * BM * 4 : size_t{0});
+                                     (c > 1 && !push) ? static_cast<size_t>(p.bpad) * BM * 4 : size_t{0});
         const int max_ctas = 512 / p.tcols;
         const size_t min_smem = static_cast<size_t>(sm_smem / (max_ctas + 1) - reserved + 1);
         return std::max(fixed + ring, min_smem);
@@ -480,6 +560,7 @@ int plan_linear(Plan *pl, int epi, const __half *W, int N, int K, const __half *
     cs = std::max(1, std::min(cs, std::min(MAX_CLUSTER, p.atoms)));
     p.cs = cs;
     p.cpr4 = cs > 1 ? ((p.bpad + cs - 1) / cs + 3) / 4 * 4 : p.bpad;
+    p.push = cs > 1 && p.bpad <= PUSH_MAX_BPAD;
     pl->smem = size_for(cs, &p.nstage);
     if (pl->smem > limit) return GPT2_B200_EINVAL;
     pl->grid = dim3(cs, p.n_tiles, 1);
