@@ -107,6 +107,20 @@ def max_over_ranks(value: float, world: int) -> float:
     return float(t.item())
 
 
+def gather_shards(out, shard, world: int) -> None:
+    """Every rank's equal-sized shard (rank order = shard_range order) into `out` on every rank: one
+    NCCL all-gather into device memory (over NVLink between the GPUs of a box); gloo (CPU tests)
+    gathers a list and concatenates."""
+    import torch
+    import torch.distributed as dist
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(out, shard)
+    else:
+        parts = [torch.empty_like(shard) for _ in range(world)]
+        dist.all_gather(parts, shard)
+        out.copy_(torch.cat(parts, dim=0))
+
+
 def barrier(world: int) -> None:
     if world > 1:
         import torch.distributed as dist
@@ -467,8 +481,7 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
                                                d_out.data_ptr(), n_steps + 1, flags, stream.cuda_stream),
                   "gpt2_b200_batch_generate")
         if gather:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(d_all, d_out)
+            gather_shards(d_all, d_out, world)
             if rank == 0:
                 h_out.copy_(d_all, non_blocking=True)
         else:

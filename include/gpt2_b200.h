@@ -257,8 +257,9 @@ int gpt2_b200_batch_generate(gpt2_b200_batch *bt, const int *d_prompt, long long
  * GPT2Backend.gemv / gpt2_gemv_fp16, cuda/kernels.cuh:94, cuda/kvcache.cu:212-214):
  * C[b, n] = epilogue(fp16(sum_k A[b, k] * W[n, k] + bias[n])) for b < B (1..256), W [N, K] row-major,
  * K a multiple of 64, bias may be NULL. epi: GPT2_B200_LINEAR_STORE writes the value, _GELU writes
- * gelu_new of it, _RESID adds it to C (the residual add). 16-byte aligned A and W, lda and ldc
- * multiples of 8. */
+ * gelu_new of it, _RESID adds it to C (the residual add). 16-byte aligned A and W, lda a multiple
+ * of 8 (A's rows are read by TMA), ldc >= N. The plan of a call (tensor maps, split) is cached per
+ * host thread for the last 16 argument sets, so a repeated call costs one launch. */
 #define GPT2_B200_LINEAR_STORE 0
 #define GPT2_B200_LINEAR_GELU 1
 #define GPT2_B200_LINEAR_RESID 2
@@ -266,7 +267,9 @@ int gpt2_b200_linear(gpt2_half *C, long long ldc, const gpt2_half *A, long long 
                      const gpt2_half *W, const gpt2_half *bias, int B, int N, int K, int epi,
                      cudaStream_t stream);
 /* The tied-head form: logits[b, n] = fp16(sum_k A[b, k] * W[n, k]) (written when logits is not NULL)
- * and d_next[b] = the first index of the row's maximum. */
+ * and d_next[b] = the first index of the row's maximum. Its per-tile argmax keys live in one buffer
+ * per device (grown on demand, never inside a stream capture): calls on one device must not overlap
+ * on the GPU. */
 int gpt2_b200_linear_argmax(gpt2_half *logits, long long ldl, const gpt2_half *A, long long lda,
                             const gpt2_half *W, int B, int N, int K, int *d_next,
                             cudaStream_t stream);

@@ -1,5 +1,6 @@
 """Multi-rank host logic on CPU (gloo, world size 2): sequence sharding has no collective on the data
-path; the only collectives are the barrier and the MAX all-reduce of per-rank timings."""
+path; the only collectives are the barrier, the MAX all-reduce of per-rank timings, and
+the gather of every rank's generated tokens into rank order."""
 import os
 import socket
 
@@ -59,3 +60,31 @@ def test_max_over_ranks_gloo_two_ranks():
     out = mgr.dict()
     mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
     assert out[0] == out[1] == pytest.approx(32.25)
+
+
+def _gather_worker(rank, world, port, out):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    total, steps = 64, 5
+    lo, hi = bench.shard_range(total, rank, world)
+    # each rank's "generated tokens": row = global sequence index * 1000 + position
+    shard = torch.tensor([[(lo + b) * 1000 + t for t in range(steps)] for b in range(hi - lo)],
+                         dtype=torch.int32)
+    full = torch.empty((total, steps), dtype=torch.int32)
+    bench.gather_shards(full, shard, world)
+    out[rank] = full.tolist()
+    dist.destroy_process_group()
+
+
+def test_token_gather_assembles_sequences_in_order():
+    port = _free_port()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_gather_worker, args=(2, port, out), nprocs=2, join=True)
+    want = [[s * 1000 + t for t in range(5)] for s in range(64)]
+    assert out[0] == want and out[1] == want
