@@ -13,6 +13,7 @@ namespace lin {
 constexpr int BM = 128;                 // weight rows (output features) per tile: the MMA's M
 constexpr int KA = 64;                  // K elements per atom: one 128-byte swizzle row
 constexpr int MAX_STAGES = 4;           // atoms in flight per CTA
+constexpr int HEAD_STAGES = 2;          // ... for the tied head (many tiles: occupancy matters more)
 constexpr int NT = 128;                 // 4 warps (one per TMEM lane quarter)
 constexpr int W_ATOM_BYTES = BM * 128;  // 16 KiB
 constexpr int MAX_BPAD = 256;           // MMA N limit

@@ -511,7 +511,9 @@ int plan_linear(Plan *pl, int epi, const __half *W, int N, int K, const __half *
         const bool push = c > 1 && p.bpad <= PUSH_MAX_BPAD;
         const size_t recv = push ? static_cast<size_t>(c) * BM * cpr4 * 4 : 0;
         const size_t fixed = 1024 + 128 + p.extra_bytes + recv;
-        int ns = std::min(MAX_STAGES, (p.atoms + c - 1) / c);
+        // The head (393 tiles of the vocabulary, no split) streams through a 2-atom ring: four CTAs
+        // fit per SM and all tiles run in one wave (20.2 -> 15.6 us for the 77 MB at B = 64).
+        int ns = std::min(epi == EPI_HEAD ? HEAD_STAGES : MAX_STAGES, (p.atoms + c - 1) / c);
         while (ns > 1 && fixed + static_cast<size_t>(ns) * stage_bytes > limit) --ns;
         *nstage = ns;
         const size_t ring = std::max(static_cast<size_t>(ns) * stage_bytes,
