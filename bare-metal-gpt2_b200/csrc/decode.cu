@@ -21,6 +21,8 @@
 #include <cstdio>
 #include <mutex>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -234,15 +236,18 @@ int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cud
     if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return GPT2_B200_ECUDA;
     if (cs != cudaStreamCaptureStatusNone) return GPT2_B200_ECAPTURE;
     if (cudaDeviceSynchronize() != cudaSuccess) return GPT2_B200_ECUDA;
+    // A grown buffer replaces the old one but the old one is never freed: a CUDA graph captured
+    // earlier keeps the address it was captured with. Growth at least doubles, so the retired
+    // buffers together stay below the live one.
     if (ctx->part_floats < floats) {
-        if (ctx->part) cudaFree(ctx->part);
+        floats = std::max(floats, 2 * ctx->part_floats);
         ctx->part = nullptr;
         ctx->part_floats = 0;
         if (cudaMalloc(&ctx->part, floats * sizeof(float)) != cudaSuccess) return GPT2_B200_ENOMEM;
         ctx->part_floats = floats;
     }
     if (ctx->counter_words < words) {
-        if (ctx->counters) cudaFree(ctx->counters);
+        words = std::max(words, 2 * ctx->counter_words);
         ctx->counters = nullptr;
         ctx->counter_words = 0;
         if (cudaMalloc(&ctx->counters, words * sizeof(unsigned)) != cudaSuccess) return GPT2_B200_ENOMEM;

@@ -868,15 +868,18 @@ static bool ensure_prefill_workspace(DeviceContext *ctx, size_t floats, size_t w
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
     if (cudaDeviceSynchronize() != cudaSuccess) return false;
+    // A grown buffer replaces the old one but the old one is never freed: a CUDA graph captured
+    // earlier keeps the address it was captured with. Growth at least doubles, so the retired
+    // buffers together stay below the live one.
     if (ctx->pf_part_floats < floats) {
-        if (ctx->pf_part) cudaFree(ctx->pf_part);
+        floats = std::max(floats, 2 * ctx->pf_part_floats);
         ctx->pf_part = nullptr;
         ctx->pf_part_floats = 0;
         if (cudaMalloc(&ctx->pf_part, floats * sizeof(float)) != cudaSuccess) return false;
         ctx->pf_part_floats = floats;
     }
     if (ctx->pf_counter_words < words) {
-        if (ctx->pf_counters) cudaFree(ctx->pf_counters);
+        words = std::max(words, 2 * ctx->pf_counter_words);
         ctx->pf_counters = nullptr;
         ctx->pf_counter_words = 0;
         if (cudaMalloc(&ctx->pf_counters, words * sizeof(unsigned)) != cudaSuccess) return false;

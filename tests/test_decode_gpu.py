@@ -88,6 +88,35 @@ def test_decode_graph_replay_with_device_length(cuda, lib, oracle, cache):
     assert lib.status() == 0
 
 
+def test_graph_survives_workspace_growth(cuda, lib, oracle, cache):
+    """A graph captured with the split-context workspace keeps working after later calls grow the
+    workspace (grown buffers are never freed while the process lives)."""
+    torch = cuda
+    lib.check(lib.gpt2_b200_reserve(1, O.H, MAXT), "reserve")
+    att = torch.empty((O.E,), dtype=torch.float16, device="cuda")
+    d_len = torch.full((1,), 700, dtype=torch.int32, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):  # one layer: 12 (layer, head) pairs, split over the context
+            lib.decode_layers(att, O.E, cache["d_q"][4], O.QKV, cache["kv"], 4, 1, d_len=d_len,
+                              max_len=MAXT, stream=s.cuda_stream)
+    torch.cuda.current_stream().wait_stream(s)
+    # grow both the partials and the counters, and use the new buffers
+    lib.check(lib.gpt2_b200_reserve(64, O.H, MAXT), "reserve")
+    lib.check(lib.gpt2_b200_reserve(8192, O.H, MAXT), "reserve")
+    other = torch.empty((3, O.E), dtype=torch.float16, device="cuda")
+    lib.decode_layers(other, O.E, cache["d_q"], O.QKV, cache["kv"], 0, 3, length=999)
+    for length in (700, 64, 1024):
+        d_len.fill_(length)
+        g.replay()
+        torch.cuda.synchronize()
+        want = oracle.decode(cache["q"][4, :O.E], cache["arena"][4, 0], cache["arena"][4, 1], length)
+        assert_close(host(att), want, f"replay after growth, len={length}")
+    assert lib.status() == 0
+
+
 def test_decode_batched_sequences(cuda, lib, oracle, cache):
     """B independent caches (here: slabs of different layers) with per-sequence lengths."""
     torch = cuda
