@@ -38,7 +38,7 @@ def _gen(cuda, seed):
 
 @pytest.mark.parametrize("epi", [G.LINEAR_STORE, G.LINEAR_GELU, G.LINEAR_RESID])
 @pytest.mark.parametrize("N,K", [(2304, 768), (768, 768), (3072, 768), (768, 3072), (40000, 768)])
-@pytest.mark.parametrize("B", [1, 5, 16, 33, 64, 200])
+@pytest.mark.parametrize("B", [1, 5, 16, 33, 64, 200, 256])
 def test_linear_matches_fp64(cuda, lib, B, N, K, epi):
     torch = cuda
     g = _gen(torch, N * 31 + K * 7 + B)
@@ -239,6 +239,39 @@ def test_batch_step_b64_matches_reference(cuda, lib, ref_gpu, weights):
             torch.cuda.synchronize()
             err = float((logits[b].float() - ref_logits.float()).abs().max())
             assert err <= LOGIT_TOL, f"step {t} seq {b}: logits differ by {err:.3e}"
+    assert lib.status() == 0
+
+
+@pytest.mark.parametrize("B", [100, 256])
+def test_batch_step_large_batches_match_reference(cuda, lib, ref_gpu, weights, B):
+    """Padded batches that do not split evenly over the cluster ranks (B = 100 -> 112 columns) and
+    the largest batch (256); sampled sequences against the reference's own step."""
+    torch = cuda
+    T, MAXT = 2, 8
+    arena, kvs = _caches(torch, B, MAXT)
+    ref_arena = torch.zeros_like(arena)
+    bt = Batch(lib, weights, kvs, B)
+    rng = np.random.default_rng(B)
+    toks = rng.integers(0, V, size=(B, T)).astype(np.int32)
+    d_tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    d_pos = torch.empty(B, dtype=torch.int32, device="cuda")
+    d_next = torch.empty(B, dtype=torch.int32, device="cuda")
+    logits = torch.empty(B, V, dtype=torch.float16, device="cuda")
+    ref_logits = torch.empty(V, dtype=torch.float16, device="cuda")
+    sample = (0, B // 3, B - 1)
+    for t in range(T):
+        d_tok.copy_(torch.from_numpy(toks[:, t]))
+        d_pos.fill_(t)
+        assert lib.gpt2_b200_batch_step(bt.h, d_tok.data_ptr(), d_pos.data_ptr(), logits.data_ptr(),
+                                        V, d_next.data_ptr(), None) == G.OK
+        torch.cuda.synchronize()
+        assert torch.equal(d_next.long(), logits.float().argmax(dim=1))
+        for b in sample:
+            ref_gpu.decode_step(ctypes.addressof(weights.struct), ref_arena[b].data_ptr(), MAXT,
+                                int(toks[b, t]), t, ref_logits.data_ptr())
+            torch.cuda.synchronize()
+            err = float((logits[b].float() - ref_logits.float()).abs().max())
+            assert err <= LOGIT_TOL, f"B={B} step {t} seq {b}: logits differ by {err:.3e}"
     assert lib.status() == 0
 
 
