@@ -52,6 +52,50 @@ int main(void) {
     assert vals[4] == ctypes.sizeof(G.GPT2Backend)
 
 
+def test_model_struct_layouts_match_reference():
+    src = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "gpt2_b200.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu\n", sizeof(GPT2LayerGPU), offsetof(GPT2LayerGPU, proj_b),
+         sizeof(GPT2WeightsGPU), offsetof(GPT2WeightsGPU, layers), offsetof(GPT2WeightsGPU, lnf_g),
+         offsetof(GPT2WeightsGPU, q), sizeof(GPT2ScratchGPU));
+  return 0;
+}'''
+    vals = [int(x) for x in _compile_c_probe(src).split()]
+    # GPT2LayerGPU: 12 half* (cuda/kernels.cuh:19-23); GPT2WeightsGPU {half*, size_t, wte, wpe,
+    # layers[12], lnf_g, lnf_b, q} (kernels.cuh:41-48); GPT2ScratchGPU 7 half* + int (kernels.cuh:54)
+    assert vals == [96, 88, 1208, 32, 1184, 1200, 64]
+    assert vals[0] == ctypes.sizeof(G.GPT2LayerGPU) and vals[2] == ctypes.sizeof(G.GPT2WeightsGPU)
+
+
+@pytest.mark.skipif(not os.path.isdir("/root/reference/cuda"), reason="reference tree not present")
+def test_header_compiles_after_the_reference_headers():
+    """A reference translation unit includes its own kernels.cuh / kvcache.cuh first, then this
+    header, and calls the drop-ins with the reference's own types (compile only)."""
+    d = tempfile.mkdtemp()
+    cu = os.path.join(d, "harness.cu")
+    open(cu, "w").write(r'''
+#include "kernels.cuh"
+#include "kvcache.cuh"
+#include "gpt2_b200.h"
+void harness(const GPT2WeightsGPU *w, GPT2KVCache *kv, GPT2ScratchGPU *s, half *att, half *qkv,
+             half *logits) {
+    GPT2Backend b = GPT2_BACKEND_NAIVE;
+    gpt2_b200_compose_backend(&b, &b);
+    b.gemv = gpt2_gemv_b200;
+    b.attention(att, qkv, 128, 768, 12, 64);
+    gpt2_attention_kv_b200(att, qkv, kv, 0, 128, 768, 12, 64);
+    gpt2_attn_decode_b200(att, qkv, kv, 0, 1);
+    gpt2_decode_step_b200(&b, w, kv, 0, 0, s, logits, nullptr);
+}
+''')
+    subprocess.run(["nvcc", "-std=c++17", "-c", "-o", os.path.join(d, "harness.o"),
+                    "-I", "/root/reference/cuda", "-I", "/root/reference/model",
+                    "-I", os.path.join(ROOT, "include"), cu], check=True, capture_output=True)
+
+
 def test_compose_backend_the_reference_way(lib):
     base = G.GPT2Backend()
     base.name = b"gemv"
