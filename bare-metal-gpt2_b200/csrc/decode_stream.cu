@@ -28,13 +28,13 @@ namespace b200 {
 namespace dstream {
 
 constexpr int HD = 64;
-constexpr int NSTAGE = 4;
+constexpr int MAX_NSTAGE = 8;
 constexpr int ROW_BYTES = HD * 2;            // 128 B per key row
 constexpr int PART_STRIDE = HD + 2;
 
 struct __align__(8) Bars {
-    uint64_t full[NSTAGE];
-    uint64_t empty[NSTAGE];
+    uint64_t full[MAX_NSTAGE];
+    uint64_t empty[MAX_NSTAGE];
     int abort;
     int is_last;
 };
@@ -43,9 +43,15 @@ struct __align__(8) Bars {
 // stage, so KPS = 8 * NCW keys and KPS * 128 bytes each of K and V per stage.
 //   NCW = 16: 128-key stages, 128 KB ring, one CTA per SM (few (job, head) pairs: the GPT-2
 //             12-layer step of one sequence, split over the context when pairs are fewer than SMs);
-//   NCW = 4:  32-key stages, 32 KB ring, six CTAs per SM (many pairs: a batch of sequences; the
-//             per-CTA ramp and tail of one pair overlap the others' streaming).
-template <int NCW>
+//   NCW = 4:  32-key stages, 3-stage 24 KB ring, eight CTAs per SM (many pairs: a batch of
+//             sequences; the per-CTA ramp and tail of one pair overlap the others' streaming).
+//             Measured at 64 sequences x 12 heads: 3 stages 5.17 / 5.96 TB/s at 512 / 1023 keys,
+//             2 stages 5.02 / 5.73, 4 stages 4.89 / 5.56, 6 stages 3.99 / 4.58 (more CTAs per SM
+//             beat a deeper ring per CTA); 2 or 8 consumer warps are slower. Launched as a
+//             programmatic dependent inside the decode step, where the next kernel's CTAs take
+//             SM slots early, the 4-stage ring (six CTAs per SM) is faster instead: attention of
+//             the 64-sequence step 249 vs 261 us, the step 658.5 vs 666.6 us.
+template <int NCW, int NSTAGE>
 struct Cfg {
     static constexpr int NT = 32 * (NCW + 1);
     static constexpr int KPS = 8 * NCW;
@@ -55,10 +61,15 @@ struct Cfg {
     static constexpr int OFF_RED = OFF_V + NSTAGE * STAGE_BYTES;  // [NCW][64] o, [NCW] m, [NCW] l
     static constexpr int OFF_BAR = OFF_RED + (NCW * HD + 2 * NCW) * 4;
     static constexpr int SMEM_BYTES = OFF_BAR + static_cast<int>(sizeof(Bars));
+    static_assert(NSTAGE >= 2 && NSTAGE <= MAX_NSTAGE, "ring depth");
     static_assert(OFF_BAR % 8 == 0, "mbarriers need 8-byte alignment");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 constexpr int NCW_FEW = 16, NCW_MANY = 4;
+constexpr int NSTAGE_FEW = 4, NSTAGE_MANY = 3, NSTAGE_MANY_CHAINED = 4;
+using CfgFew = Cfg<NCW_FEW, NSTAGE_FEW>;
+using CfgMany = Cfg<NCW_MANY, NSTAGE_MANY>;
+using CfgManyChained = Cfg<NCW_MANY, NSTAGE_MANY_CHAINED>;
 
 struct Params {
     const __half *q;
@@ -88,9 +99,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsign
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int NCW>
+template <int NCW, int NSTAGE>
 __global__ void __launch_bounds__(32 * (NCW + 1)) k_decode_stream(const Params p) {
-    using C = Cfg<NCW>;
+    using C = Cfg<NCW, NSTAGE>;
     constexpr int KPS = C::KPS, STAGE_BYTES = C::STAGE_BYTES;
     constexpr int OFF_K = C::OFF_K, OFF_V = C::OFF_V, OFF_RED = C::OFF_RED, OFF_BAR = C::OFF_BAR;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -342,8 +353,8 @@ int decode_stream_splits(int max_len, long long pairs, int num_sms) {
     const int sms = num_sms > 0 ? num_sms : 148;
     long long n = (sms + pairs / 2) / pairs;  // round(sms / pairs)
     if (n < 1) n = 1;
-    const long long max_n = (max_len + dstream::Cfg<dstream::NCW_FEW>::KPS - 1) /
-                            dstream::Cfg<dstream::NCW_FEW>::KPS;
+    const long long max_n = (max_len + dstream::CfgFew::KPS - 1) /
+                            dstream::CfgFew::KPS;
     if (n > max_n) n = max_n;
     return static_cast<int>(n);
 }
@@ -354,12 +365,16 @@ int prepare_decode_stream() {
     DeviceContext *ctx = device_context();
     if (!ctx) return GPT2_B200_ECUDA;
     if (!ctx->decode_attr_done) {
-        if (cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_FEW>,
+        if (cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_FEW, dstream::NSTAGE_FEW>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 dstream::Cfg<dstream::NCW_FEW>::SMEM_BYTES) != cudaSuccess ||
-            cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_MANY>,
+                                 dstream::CfgFew::SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 dstream::Cfg<dstream::NCW_MANY>::SMEM_BYTES) != cudaSuccess)
+                                 dstream::CfgMany::SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(
+                dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY_CHAINED>,
+                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                dstream::CfgManyChained::SMEM_BYTES) != cudaSuccess)
             return GPT2_B200_ECUDA;
         ctx->decode_attr_done = true;
     }
@@ -409,17 +424,21 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
     cfg.gridDim = dim3(p.nsplit, H, njobs);
     // Many (job, head) pairs, each whole in one CTA: the small CTA shape, several per SM.
     const bool many = p.nsplit == 1 && static_cast<long long>(njobs) * H >= 2LL * ctx->num_sms;
-    cfg.blockDim = dim3(many ? dstream::Cfg<dstream::NCW_MANY>::NT : dstream::Cfg<dstream::NCW_FEW>::NT, 1, 1);
-    cfg.dynamicSmemBytes = many ? dstream::Cfg<dstream::NCW_MANY>::SMEM_BYTES
-                                : dstream::Cfg<dstream::NCW_FEW>::SMEM_BYTES;
+    cfg.blockDim = dim3(many ? dstream::CfgMany::NT : dstream::CfgFew::NT, 1, 1);
+    cfg.dynamicSmemBytes = !many ? dstream::CfgFew::SMEM_BYTES
+                           : pdl ? dstream::CfgManyChained::SMEM_BYTES
+                                 : dstream::CfgMany::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    const cudaError_t err = many ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY>, p)
-                                 : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW>, p);
+    const cudaError_t err =
+        !many ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW, dstream::NSTAGE_FEW>, p)
+        : pdl ? cudaLaunchKernelEx(
+                    &cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY_CHAINED>, p)
+              : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>, p);
     return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 
