@@ -402,9 +402,14 @@ int gpt2_b200_batch_create(gpt2_b200_batch **out, const GPT2WeightsGPU *w, const
 
 void gpt2_b200_batch_destroy(gpt2_b200_batch *bt) {
     if (!bt) return;
+    // replays queued on any stream may still be running: drain the device before releasing them
+    int prev = -1;
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != bt->device) cudaSetDevice(bt->device);
+    cudaDeviceSynchronize();
     for (cudaGraphExec_t &g : bt->graph)
         if (g) cudaGraphExecDestroy(g);
     if (bt->arena) cudaFree(bt->arena);
+    if (prev >= 0 && prev != bt->device) cudaSetDevice(prev);
     delete bt;
 }
 
@@ -446,6 +451,8 @@ int gpt2_b200_batch_generate(gpt2_b200_batch *bt, const int *d_prompt, long long
     // The graph bakes in the generation buffers; re-capture when they change.
     if (bt->graph[gi] && (bt->g_prompt != d_prompt || bt->g_plen != d_plen || bt->g_out != d_out ||
                           bt->g_ps != prompt_stride || bt->g_os != out_stride)) {
+        // earlier replays of these graphs may still be queued: let them finish first
+        if (cudaDeviceSynchronize() != cudaSuccess) return GPT2_B200_ECUDA;
         for (cudaGraphExec_t &g : bt->graph)
             if (g) {
                 cudaGraphExecDestroy(g);
