@@ -233,6 +233,7 @@ void gpt2_decode_step_b200(const GPT2Backend *be, const GPT2WeightsGPU *w, GPT2K
 typedef struct gpt2_b200_batch gpt2_b200_batch;
 int gpt2_b200_batch_create(gpt2_b200_batch **out, const GPT2WeightsGPU *w, const GPT2KVCache *kvs,
                            int B);
+/* Releases the batch; synchronises its device first (replays may still be queued). */
 void gpt2_b200_batch_destroy(gpt2_b200_batch *bt);
 
 /* One decode step: sequence b consumes d_tokens[b] at position d_pos[b] (device ints), appends its
