@@ -152,6 +152,32 @@ def test_decode_rejects_bad_arguments(lib):
     assert lib.gpt2_b200_last_error() == G.EINVAL
 
 
+def test_model_entry_points_reject_bad_arguments(lib):
+    """The decode-step and linear-layer entry points refuse bad arguments before any CUDA call."""
+    w = G.GPT2WeightsGPU()  # every pointer NULL
+    kvs = (G.GPT2KVCache * 2)(G.cache_view(4096, 12, 64), G.cache_view(8192, 12, 64))
+    h = ctypes.c_void_p()
+    assert lib.gpt2_b200_batch_create(ctypes.byref(h), ctypes.byref(w), kvs, 2) == G.EINVAL
+    assert lib.gpt2_b200_batch_create(None, ctypes.byref(w), kvs, 2) == G.EINVAL
+    assert lib.gpt2_b200_batch_create(ctypes.byref(h), None, kvs, 2) == G.EINVAL
+    assert not h.value
+    assert lib.gpt2_b200_batch_step(None, 16, 16, None, 0, None, None) == G.EINVAL
+    assert lib.gpt2_b200_batch_generate(None, 16, 512, 16, 8, 16, 9, 0, None) == G.EINVAL
+    assert lib.gpt2_b200_batch_launches_per_step(None, 0) == -1
+    lib.gpt2_b200_batch_destroy(None)  # no-op
+    # linear: unknown epilogue, output stride below N
+    assert lib.gpt2_b200_linear(16, 768, 16, 768, 16, None, 4, 768, 768, 7, None) == G.EINVAL
+    assert lib.gpt2_b200_linear(16, 100, 16, 768, 16, None, 4, 768, 768, 0, None) == G.EINVAL
+    assert lib.gpt2_b200_linear(None, 768, 16, 768, 16, None, 4, 768, 768, 0, None) == G.EINVAL
+    assert lib.gpt2_b200_linear_argmax(None, 0, 16, 768, 16, 4, 768, 768, None, None) == G.EINVAL
+    # the decode-step drop-in: kv->len must equal pos (the reference's precondition)
+    kv = G.cache_view(4096, 12, 64, length=3)
+    lib.gpt2_decode_step_b200(None, ctypes.byref(w), ctypes.byref(kv), 1, 5, None, None, None)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+    lib.gpt2_decode_step_b200(None, ctypes.byref(w), ctypes.byref(kv), -1, 3, None, None, None)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+
+
 def test_kv_writers_reject_bad_positions(lib):
     kv = G.cache_view(4096, 12, 64)
     assert lib.gpt2_kv_append_b200_stream(ctypes.byref(kv), 0, 1, 16, 0, None, 64, None) == G.EINVAL
