@@ -47,10 +47,7 @@ struct __align__(8) Bars {
 //             sequences; the per-CTA ramp and tail of one pair overlap the others' streaming).
 //             Measured at 64 sequences x 12 heads: 3 stages 5.17 / 5.96 TB/s at 512 / 1023 keys,
 //             2 stages 5.02 / 5.73, 4 stages 4.89 / 5.56, 6 stages 3.99 / 4.58 (more CTAs per SM
-//             beat a deeper ring per CTA); 2 or 8 consumer warps are slower. Launched as a
-//             programmatic dependent inside the decode step, where the next kernel's CTAs take
-//             SM slots early, the 4-stage ring (six CTAs per SM) is faster instead: attention of
-//             the 64-sequence step 249 vs 261 us, the step 658.5 vs 666.6 us.
+//             beat a deeper ring per CTA); 2 or 8 consumer warps are slower.
 template <int NCW, int NSTAGE>
 struct Cfg {
     static constexpr int NT = 32 * (NCW + 1);
@@ -66,10 +63,9 @@ struct Cfg {
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 constexpr int NCW_FEW = 16, NCW_MANY = 4;
-constexpr int NSTAGE_FEW = 4, NSTAGE_MANY = 3, NSTAGE_MANY_CHAINED = 4;
+constexpr int NSTAGE_FEW = 4, NSTAGE_MANY = 3;
 using CfgFew = Cfg<NCW_FEW, NSTAGE_FEW>;
 using CfgMany = Cfg<NCW_MANY, NSTAGE_MANY>;
-using CfgManyChained = Cfg<NCW_MANY, NSTAGE_MANY_CHAINED>;
 
 struct Params {
     const __half *q;
@@ -370,11 +366,7 @@ int prepare_decode_stream() {
                                  dstream::CfgFew::SMEM_BYTES) != cudaSuccess ||
             cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 dstream::CfgMany::SMEM_BYTES) != cudaSuccess ||
-            cudaFuncSetAttribute(
-                dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY_CHAINED>,
-                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                dstream::CfgManyChained::SMEM_BYTES) != cudaSuccess)
+                                 dstream::CfgMany::SMEM_BYTES) != cudaSuccess)
             return GPT2_B200_ECUDA;
         ctx->decode_attr_done = true;
     }
@@ -425,9 +417,7 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
     // Many (job, head) pairs, each whole in one CTA: the small CTA shape, several per SM.
     const bool many = p.nsplit == 1 && static_cast<long long>(njobs) * H >= 2LL * ctx->num_sms;
     cfg.blockDim = dim3(many ? dstream::CfgMany::NT : dstream::CfgFew::NT, 1, 1);
-    cfg.dynamicSmemBytes = !many ? dstream::CfgFew::SMEM_BYTES
-                           : pdl ? dstream::CfgManyChained::SMEM_BYTES
-                                 : dstream::CfgMany::SMEM_BYTES;
+    cfg.dynamicSmemBytes = many ? dstream::CfgMany::SMEM_BYTES : dstream::CfgFew::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -435,10 +425,8 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     const cudaError_t err =
-        !many ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW, dstream::NSTAGE_FEW>, p)
-        : pdl ? cudaLaunchKernelEx(
-                    &cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY_CHAINED>, p)
-              : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>, p);
+        many ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>, p)
+             : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW, dstream::NSTAGE_FEW>, p);
     return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 
