@@ -246,6 +246,51 @@ class ModelWeights:
         self.struct = w
 
 
+class DecodeBatch:
+    """B sequences of GPT-2-124M decoded together (the gpt2_b200_batch_* entry points).
+
+    caches: a torch fp16 tensor [B][12][2][12][maxT][64] (each sequence's arena in the reference
+    layout) that stays alive as long as the batch. step() consumes one token per sequence at its
+    position; generate() runs lock-step greedy generation (prompt tokens first) in a CUDA graph.
+    """
+
+    def __init__(self, lib: "Lib", weights: ModelWeights, caches):
+        self.lib, self.weights, self.caches = lib, weights, caches
+        self.B, max_t = int(caches.shape[0]), int(caches.shape[4])
+        self.kvs = (GPT2KVCache * self.B)(*[cache_view(caches[b].data_ptr(), N_LAYER, max_t)
+                                             for b in range(self.B)])
+        self.h = ctypes.c_void_p()
+        lib.check(lib.gpt2_b200_batch_create(ctypes.byref(self.h), ctypes.byref(weights.struct),
+                                             self.kvs, self.B), "gpt2_b200_batch_create")
+
+    def step(self, tokens, positions, logits=None, next_tokens=None, stream: int = 0) -> None:
+        """tokens, positions: int32 device tensors [B]; logits: fp16 [B][>= VOCAB] or None;
+        next_tokens: int32 [B] or None (argmax of each row)."""
+        self.lib.check(self.lib.gpt2_b200_batch_step(
+            self.h, tokens.data_ptr(), positions.data_ptr(),
+            logits.data_ptr() if logits is not None else None,
+            logits.stride(0) if logits is not None else 0,
+            next_tokens.data_ptr() if next_tokens is not None else None, stream),
+            "gpt2_b200_batch_step")
+
+    def generate(self, prompt, prompt_len, n_steps: int, out, stream: int = 0) -> None:
+        """prompt: int32 [B][P]; prompt_len: int32 [B] (1..P); out: int32 [B][>= n_steps+1]."""
+        self.lib.check(self.lib.gpt2_b200_batch_generate(
+            self.h, prompt.data_ptr(), prompt.stride(0), prompt_len.data_ptr(), n_steps,
+            out.data_ptr(), out.stride(0), 0, stream), "gpt2_b200_batch_generate")
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.gpt2_b200_batch_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
 def _numel(shape) -> int:
     n = 1
     for d in shape:

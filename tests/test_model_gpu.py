@@ -380,6 +380,33 @@ def test_generate_matches_host_driven_steps(cuda, lib, weights):
     assert lib.status() == 0
 
 
+def test_decode_batch_wrapper_generates_like_the_steps(cuda, lib, weights):
+    """The Python DecodeBatch wrapper: generate() equals step() driven from the host."""
+    torch = cuda
+    B, MAXT, N_STEPS = 3, 32, 10
+    caches = torch.zeros(B, G.N_LAYER, 2, G.N_HEAD, MAXT, 64, dtype=torch.float16, device="cuda")
+    batch = G.DecodeBatch(lib, weights, caches)
+    prompt = torch.randint(0, V, (B, 8), dtype=torch.int32, device="cuda")
+    plen = torch.tensor([1, 4, 8], dtype=torch.int32, device="cuda")
+    out = torch.empty(B, N_STEPS + 1, dtype=torch.int32, device="cuda")
+    batch.generate(prompt, plen, N_STEPS, out)
+    torch.cuda.synchronize()
+    caches.zero_()
+    tok = prompt[:, 0].clone()
+    pos = torch.zeros(B, dtype=torch.int32, device="cuda")
+    nxt = torch.empty(B, dtype=torch.int32, device="cuda")
+    want = [prompt[:, 0].cpu().tolist()]
+    for t in range(N_STEPS):
+        pos.fill_(t)
+        batch.step(tok, pos, next_tokens=nxt)
+        row = [int(prompt[b, t + 1]) if t + 1 < int(plen[b]) else int(nxt[b]) for b in range(B)]
+        want.append(row)
+        tok.copy_(torch.tensor(row, dtype=torch.int32))
+    assert out.cpu().t().tolist() == want
+    batch.close()
+    assert lib.status() == 0
+
+
 def test_batch_rejects_bad_arguments(cuda, lib, weights):
     torch = cuda
     arena, kvs = _caches(torch, 2, 32)
