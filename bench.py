@@ -687,7 +687,7 @@ def main(argv=None):
                     d = bench_decode_batched(torch, lib, 20, args.warmup, world, rank, c, seed=800 + rank)
                     d["roofline"] = {"bound": "hbm", "achieved": d["kv_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
                                      "unit": "GB/s", "frac": d["kv_gbs_per_gpu"] / peaks["hbm_gbs"],
-                                     "kernel": "k_decode_stream<4>"}
+                                     "kernel": "k_decode_stream<4, 3>"}
                     sec[f"decode_B64_ctx{c}"] = d
             if "per_layer" in legs:
                 sec["prefill_per_layer_launches"] = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
