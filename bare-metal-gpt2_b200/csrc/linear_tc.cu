@@ -14,9 +14,12 @@
 //                  released by tcgen05.commit to its "empty" mbarrier;
 //   warps 0-3      epilogue: one thread per weight row (TMEM lane), tcgen05.ld of the batch columns.
 // When the tiles alone would leave SMs idle, the K range of a tile is split across the CTAs of a
-// thread-block cluster. Each CTA writes its fp32 partial tile to its own shared memory, a cluster
-// barrier publishes it, and CTA r reduces columns [r*c, (r+1)*c) over all ranks in rank order
-// through distributed shared memory (deterministic; nothing goes through global memory).
+// thread-block cluster, CTA r owning batch columns [r*c, (r+1)*c). Small batches (padded B <= 32):
+// each CTA stores its partial columns straight into the owners' receive buffers (plain distributed-
+// shared-memory stores), one cluster barrier publishes them and each owner sums locally. Larger
+// batches: each CTA stages its partial tile in its own shared memory, a cluster barrier publishes
+// it, and the owners read their columns from the peers. Either way the ranks' partials are summed
+// in rank order (deterministic) and nothing goes through global memory.
 //
 // Epilogues (fused, so no separate bias / GELU / residual / append launch): see lin::Epi. The
 // rounding follows the reference: h = fp16(acc + bias) as k_gemv_fp16 writes it, then GELU (k_gelu,
