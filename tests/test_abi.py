@@ -190,3 +190,47 @@ def test_kv_writers_reject_bad_positions(lib):
 def test_strerror_and_version(lib):
     assert lib.gpt2_b200_strerror(G.ETIMEOUT) == b"a kernel wait timed out"
     assert b"sm_100a" in lib.gpt2_b200_version()
+
+
+def test_argmax_key_orders_like_an_argmax_over_fp16_logits():
+    """The head's per-tile argmax keys (csrc/linear.cuh argmax_key): a larger fp16 value always wins,
+    equal values go to the smaller index (first occurrence), and the index is recovered exactly.
+    Checked on the host build of the same inline function over random and edge values."""
+    import numpy as np
+    d = tempfile.mkdtemp()
+    src = os.path.join(d, "keys.cu")
+    open(src, "w").write(r'''
+#include <cstdio>
+#include "linear.cuh"
+int main() {
+    float v; unsigned n;
+    while (std::scanf("%f %u", &v, &n) == 2)
+        std::printf("%llu %d\n", b200::lin::argmax_key(v, n), b200::lin::argmax_key_index(b200::lin::argmax_key(v, n)));
+    return 0;
+}
+''')
+    exe = os.path.join(d, "keys")
+    subprocess.run(["nvcc", "-std=c++17", "-o", exe, "-I", os.path.join(ROOT, "include"),
+                    "-I", os.path.join(ROOT, "bare-metal-gpt2_b200", "csrc"), src], check=True,
+                   capture_output=True)
+    rng = np.random.default_rng(5)
+    vals = np.concatenate([rng.standard_normal(400).astype(np.float16).astype(np.float32),
+                           np.array([0.0, -0.0, 65504.0, -65504.0, 6e-8, -6e-8, 1.0, 1.0, -1.0, -1.0],
+                                    dtype=np.float32)])
+    idx = rng.permutation(50257)[:len(vals)].astype(np.uint32)
+    inp = "".join(f"{v!r} {i}\n" for v, i in zip(vals.tolist(), idx.tolist()))
+    out = subprocess.run([exe], input=inp, capture_output=True, text=True, check=True).stdout.split()
+    keys = [int(x) for x in out[0::2]]
+    back = [int(x) for x in out[1::2]]
+    assert back == idx.tolist()
+    # the winner of every pair is the argmax rule's winner (value first, then the lower index);
+    # +0.0 and -0.0 compare by bit pattern here (+0 wins), which only matters for exact zeros
+    for a in range(0, len(vals), 7):
+        for b in range(len(vals)):
+            va, vb = vals[a], vals[b]
+            if va == vb and va == 0.0:
+                continue
+            want_a = va > vb or (va == vb and idx[a] < idx[b])
+            if a == b:
+                continue
+            assert (keys[a] > keys[b]) == want_a, (va, vb, idx[a], idx[b])
