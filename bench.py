@@ -555,6 +555,34 @@ def cpu_reference_sample(seconds: float, max_layers: int | None = None):
             "tflops": 2.0 * P * P * E / per_layer / 1e12}
 
 
+def cpu_decode_sample(ctx: int, seconds: float):
+    """CPU baseline of configs[2]: the reference has no CPU M=1 attention, so this times the oracle's
+    restatement of its decode kernel (k_attn_decode, cuda/kvcache.cu:88-129: double accumulation,
+    OpenMP over the 12 heads) for the 12 layers of one step at context `ctx`, until `seconds` of work.
+    Reported in the configs' KV-byte convention (fp16 bytes, gpt2_kv_step_bytes)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    orc = O.Oracle()
+    rng = np.random.default_rng(77)
+    kv = rng.standard_normal((LAYERS, 2, H, MAXT, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    q = rng.standard_normal((LAYERS, E), dtype=np.float32).astype(np.float16).astype(np.float32)
+
+    def step():
+        for L in range(LAYERS):
+            orc.decode(q[L], kv[L, 0], kv[L, 1], ctx)
+    step()
+    times, t_end = [], time.perf_counter() + seconds
+    while len(times) < 3 or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    per_step = statistics.median(times)
+    return {"value": decode_bytes(ctx) / per_step / 1e9, "unit": "GB/s", "cores": orc.threads(),
+            "kind": "port", "us_per_step": per_step * 1e6,
+            "sample": f"{len(times)} 12-layer steps at ctx {ctx} (median), the oracle's double-precision "
+                      "restatement of k_attn_decode (the reference has no CPU decode attention)"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU attention on this host's cores, same metric/config."""
     if rank != 0:
@@ -719,6 +747,10 @@ def main(argv=None):
                                     "sample": f"{cpu['layers']} single-layer P=1024 attention calls "
                                               f"(median {cpu['per_layer_s'] * 1e3:.1f} ms each), "
                                               "scaled to TFLOP/s"}
+            for c in (128, 512, 1023):
+                key = f"decode_ctx{c}"
+                if key in sec:
+                    sec[key]["cpu_baseline"] = cpu_decode_sample(c, 1.0)
     if rank == 0:
         emit(line)
     if world > 1:
