@@ -40,6 +40,20 @@ thread_local int t_last_error = GPT2_B200_OK;
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
+EncodeTiledFn tensor_map_encoder() {
+    // function-local static: initialised once, thread-safe
+    static const EncodeTiledFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<EncodeTiledFn>(ptr);
+        return static_cast<EncodeTiledFn>(nullptr);
+    }();
+    return fn;
+}
+
 DeviceContext *device_context() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;

@@ -47,6 +47,14 @@ struct DeviceContext {
 
 // Returns the context of the current device (creating it on first use), or nullptr on CUDA error.
 DeviceContext *device_context();
+
+// The driver's cuTensorMapEncodeTiled, looked up once through the runtime (nullptr when the driver
+// lacks it). Shared by every kernel that builds TMA tensor maps.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
 unsigned long long wait_timeout_ns();
 void set_last_error(int code);
 

@@ -411,31 +411,11 @@ __global__ void __launch_bounds__(NT, 1) k_linear_tc(const __grid_constant__ CUt
 // ---------------------------------------------------------------- host side
 namespace {
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
-                                             cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
-    return fn;
-}
-
 // 2-D fp16 map over rows x cols (row stride ld elements), box 64 x box_rows, 128-byte swizzle.
 // Rows past `rows` read as zero.
 bool encode_rows(CUtensorMap *m, const __half *ptr, long long rows, int cols, long long ld,
                  int box_rows) {
-    EncodeTiledFn fn = encode_fn();
+    EncodeTiledFn fn = tensor_map_encoder();
     if (!fn) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};

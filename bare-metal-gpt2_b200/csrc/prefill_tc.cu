@@ -777,25 +777,6 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
 }
 
 // ------------------------------------------------------------------ host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
-                                             cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
-    return fn;
-}
 
 // Chunk size (K/V tiles per work unit) for a launch of n_pairs pairs per (head, sequence) on `sms`
 // SMs. Time model in units of one K/V tile step of a pair (both query tiles): a CTA's share of the
@@ -896,7 +877,7 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     using namespace prefill;
     DeviceContext *ctx = device_context();
     if (!ctx) return GPT2_B200_ECUDA;
-    EncodeTiledFn enc = encode_fn();
+    EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return GPT2_B200_EDEVICE;
     if (!ctx->prefill_attr_done) {
         for (auto fn : {k_flash_prefill_tc<false>, k_flash_prefill_tc<true>}) {
