@@ -103,7 +103,6 @@ __global__ void __launch_bounds__(NT, 1) k_linear_tc(const __grid_constant__ CUt
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int stage_bytes = W_ATOM_BYTES + p.bpad * 128;
-    // The ring; after the last MMA the split-K path reuses it for the partial tile [bpad][128].
     // The stage ring; the pull reduction reuses it for the partial tile [bpad][128] after the MMAs.
     const int ring = max(p.nstage * stage_bytes, (p.cs > 1 && !p.push) ? p.bpad * BM * 4 : 0);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + ring);

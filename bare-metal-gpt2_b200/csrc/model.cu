@@ -3,15 +3,17 @@
 // The reference's step (gpt2_decode_step_cuda, cuda/kvcache.cu:233-269) decodes ONE sequence with
 // 135 launches: embed; per layer LayerNorm, QKV GEMV, K/V append, attention, projection GEMV, add,
 // LayerNorm, FC GEMV, GELU, projection GEMV, add; final LayerNorm; tied-head GEMV. Here one step
-// serves B sequences and each layer is six launches:
+// serves B sequences and each layer is seven launches:
 //   QKV linear   (bias; K/V appended to each sequence's cache at its position in the epilogue)
-//   attention    (the batched split-context decode kernel, one launch for all B x 12 heads)
+//   attention    (the batched decode kernel, one launch for all B x 12 heads)
 //   projection   (bias + residual add into x)
 //   LayerNorm 2
 //   FC linear    (bias + GELU)
-//   projection   (bias + residual add into x), then LayerNorm 1 of the next layer (or the final one)
+//   projection   (bias + residual add into x)
+//   LayerNorm 1 of the next layer (or the final one)
 // The embedding kernel also applies layer 0's LayerNorm, and the head's epilogue turns the logits
-// into per-tile argmax keys that one small kernel reduces to the next token. A lock-step greedy
+// into per-tile argmax keys that one small kernel reduces to the next token: 1 + 12 x 7 + 2 = 87
+// launches per step (gpt2_b200_batch_launches_per_step reports the count). A lock-step greedy
 // generator captures the whole step, token selection included, in one CUDA graph.
 //
 // Arithmetic follows the reference's fp16 path: activations stored in fp16, fp32 accumulation,
