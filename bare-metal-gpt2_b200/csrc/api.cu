@@ -64,7 +64,9 @@ DeviceContext *device_context() {
     if (g_ctx_ready[dev]) return t_ctx[dev] = &g_ctx[dev];
     if (g_ctx_err[dev]) return nullptr;
     cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10) {
+    // The library is built for sm_100a only: arch-specific code runs on compute capability 10.0
+    // alone (not 10.3 and the like), so any other part fails here rather than at its first launch.
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10 || prop.minor != 0) {
         g_ctx_err[dev] = GPT2_B200_EDEVICE;
         return nullptr;
     }
@@ -311,7 +313,7 @@ const char *gpt2_b200_strerror(int code) {
         case GPT2_B200_EINVAL: return "invalid argument";
         case GPT2_B200_ECUDA: return "CUDA runtime error";
         case GPT2_B200_ENOMEM: return "allocation refused";
-        case GPT2_B200_EDEVICE: return "device is not sm_100 or lacks tensor-map support";
+        case GPT2_B200_EDEVICE: return "device is not compute capability 10.0 (sm_100) or lacks tensor-map support";
         case GPT2_B200_ETIMEOUT: return "a kernel wait timed out";
         case GPT2_B200_ECAPTURE: return "allocation needed while the stream is being captured";
         default: return "unknown";

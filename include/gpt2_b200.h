@@ -40,7 +40,7 @@ typedef struct { unsigned short bits; } gpt2_half;
 #define GPT2_B200_EINVAL 1      /* bad argument (shape, alignment, length, null pointer) */
 #define GPT2_B200_ECUDA 2       /* a CUDA runtime call failed */
 #define GPT2_B200_ENOMEM 3      /* allocation refused (cache plan over budget, workspace) */
-#define GPT2_B200_EDEVICE 4     /* the device is not an sm_100 part, or the driver lacks TMA */
+#define GPT2_B200_EDEVICE 4     /* the device is not compute capability 10.0, or the driver lacks TMA */
 #define GPT2_B200_ETIMEOUT 5    /* a kernel's bounded wait expired (see gpt2_b200_status) */
 #define GPT2_B200_ECAPTURE 6    /* would need to allocate while the stream is being captured */
 
