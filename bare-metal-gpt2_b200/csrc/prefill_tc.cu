@@ -753,6 +753,11 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         tmem_alloc(&bars->tmem_base, TMEM_COLS);
         tmem_relinquish();
     }
+    // Launched as a programmatic dependent: the set-up above touches no global memory, so it overlaps
+    // the previous kernel's tail; every global access (inputs, output, cache, workspace) follows this
+    // wait. Dependents may start placing CTAs at once (they wait the same way before any access).
+    grid_dependency_wait();
+    grid_launch_dependents();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -986,12 +991,20 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     p.timeout_ns = wait_timeout_ns();
     // Persistent: at most CTAS_PER_SM resident CTAs per SM, each looping over its share of items.
     const long long slots = static_cast<long long>(CTAS_PER_SM) * (ctx->num_sms > 0 ? ctx->num_sms : 148);
-    const unsigned grid = static_cast<unsigned>(total < slots ? total : slots);
-    if (p.units_per_hb != p.n_pairs)
-        k_flash_prefill_tc<true><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, tm_kv, p);
-    else
-        k_flash_prefill_tc<false><<<grid, NTHREADS, SMEM_BYTES, stream>>>(tm, tm_att, tm_kv, p);
-    return cudaGetLastError() == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(total < slots ? total : slots));
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = p.units_per_hb != p.n_pairs
+                                ? cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<true>, tm, tm_att, tm_kv, p)
+                                : cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<false>, tm, tm_att, tm_kv, p);
+    return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 
 }  // namespace b200
