@@ -748,6 +748,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         tma_prefetch_desc(&tm_qkv);
         tma_prefetch_desc(&tm_att);
         if (p.kv_fill) tma_prefetch_desc(&tm_kv);
+        // The first item's Q tiles and its first K and V tiles into L2 while the previous kernel
+        // drains (the producer's first loads, issued after the dependency wait, then hit L2).
+        Item i0;
+        if (get_item<kSplit>(p, 0, i0)) {
+            for (int t = 0; t < (i0.nk[1] ? 2 : 1); ++t)
+                tma_prefetch_l2_3d(&tm_qkv, i0.h * HD, (2 * i0.pair + t) * BM, i0.b);
+            tma_prefetch_l2_3d(&tm_qkv, p.E + i0.h * HD, i0.kv0 * BN, i0.b);
+            tma_prefetch_l2_3d(&tm_qkv, 2 * p.E + i0.h * HD, i0.kv0 * BN, i0.b);
+        }
     }
     if (warp == 1) {
         tmem_alloc(&bars->tmem_base, TMEM_COLS);

@@ -140,6 +140,15 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// Prefetch of one 3-D box into L2 (no shared memory, no completion to wait for). It only warms L2,
+// which is coherent for the whole GPU, so it may run before a grid dependency wait: a later load still
+// returns what the producing kernel wrote.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap *map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
