@@ -41,6 +41,10 @@
 // TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 224.5 KB
 // (Q 64 KB, K and V rings 128 KB, output slots 32 KB, barriers). No cluster, no multicast. Every
 // mbarrier wait is bounded.
+//
+// Launch: a programmatic dependent of the previous kernel in the stream. Barrier init, TMEM
+// allocation and an L2 prefetch of the first item's Q, K and V tiles overlap that kernel's tail;
+// every load, store and workspace access follows the grid dependency wait.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
