@@ -36,6 +36,7 @@ sys.path.insert(0, os.path.join(ROOT, "bare-metal-gpt2_b200"))
 
 E, H, D, QKV, LAYERS = 768, 12, 64, 2304, 12
 P = 1024
+METRIC = "prefill attn TFLOP/s @P=1024 (12 layers, causal)"  # both arms report this metric
 CTX = 1023
 MAXT = 1024
 L2_BYTES = 126 * 1024 * 1024
@@ -611,7 +612,7 @@ def run_reference(args, rank, world):
     ms_step = dt / args.steps * 1e3
     value = layers * 2.0 * P * P * E / (dt / args.steps) / 1e12
     sample = f"{layers} of 12 layers (P=1024, fp16-rounded N(0,1) qkv) per step"
-    line = {"impl": "reference", "metric": "prefill attn TFLOP/s @P=1024 (12 layers, causal)",
+    line = {"impl": "reference", "metric": METRIC,
             "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate over fp32",
@@ -673,7 +674,7 @@ def main(argv=None):
     traffic = profile_traffic("prefill_tc_P1024_L12")
 
     line = {
-        "metric": "prefill attn TFLOP/s @P=1024 (12 layers, causal)",
+        "metric": METRIC,
         "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": region / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
