@@ -163,11 +163,15 @@ class Lib:
 
     # -------------------------------------------------------------- checked helpers
     def check(self, rc: int, what: str) -> None:
+        """Raises RuntimeError with the library's message for any return code other than OK."""
         if rc != OK:
             raise RuntimeError(f"{what}: {self.lib.gpt2_b200_strerror(rc).decode()} ({rc})")
 
     def prefill(self, att, qkv, T: int, B: int = 1, stream: int = 0, qkv_stride: int = 0,
                 att_stride: int = 0, E: int = 768, H: int = 12) -> None:
+        """Causal prefill attention of B sequences (or layers) of T rows: att[b] from qkv[b] as the
+        reference's attention slot computes it (cuda/kernels_fused.cu:145-149, one launch for all B).
+        Strides are in elements, 0 for packed rows."""
         rc = self.lib.gpt2_attention_b200_batched(att.data_ptr(), qkv.data_ptr(), B, T, E, H, 64,
                                                   qkv_stride, att_stride, stream)
         self.check(rc, "gpt2_attention_b200_batched")
@@ -175,12 +179,15 @@ class Lib:
     def decode_layers(self, att, att_stride: int, q, q_stride: int, kv: GPT2KVCache, L0: int,
                       nL: int, length: int = 0, d_len=None, max_len: int = 0,
                       stream: int = 0) -> None:
+        """M=1 decode attention of layers L0..L0+nL-1 over the first `length` cache positions (or the
+        device int `d_len`), one launch: gpt2_attn_decode (cuda/kvcache.cu:207-210) for many layers."""
         rc = self.lib.gpt2_attn_decode_b200_layers(
             att.data_ptr(), att_stride, q.data_ptr(), q_stride, ctypes.byref(kv), L0, nL,
             d_len.data_ptr() if d_len is not None else None, length, max_len, stream)
         self.check(rc, "gpt2_attn_decode_b200_layers")
 
     def status(self, clear: bool = True) -> int:
+        """The device's status word (bounded-wait timeouts and bad-input bits), cleared if asked."""
         return int(self.lib.gpt2_b200_status(1 if clear else 0))
 
 
@@ -280,6 +287,7 @@ class DecodeBatch:
             out.data_ptr(), out.stride(0), 0, stream), "gpt2_b200_batch_generate")
 
     def close(self) -> None:
+        """Destroys the batch (the library synchronises the device first); safe to call twice."""
         if self.h:
             self.lib.gpt2_b200_batch_destroy(self.h)
             self.h = ctypes.c_void_p()
@@ -302,6 +310,7 @@ _LIB: Lib | None = None
 
 
 def load() -> Lib:
+    """The process-wide Lib; raises if lib/libgpt2_b200.so is missing (there is no fallback)."""
     global _LIB
     if _LIB is None:
         _LIB = Lib()
