@@ -213,8 +213,8 @@ int gpt2_kv_scatter_prefill_b200_stream(GPT2KVCache *kv, int L, const gpt2_half 
  * every weight matmul is one tcgen05 pass over the weights for all B rows with bias, GELU, residual
  * add and the K/V append fused into its epilogue, the attention is the batched decode kernel above,
  * and the head's epilogue reduces the logits to per-sequence argmax keys. Four weight launches, one
- * attention launch and one LayerNorm launch per layer. GPT-2-124M shapes only (E 768, 12 layers,
- * 12 heads, vocabulary 50257). */
+ * attention launch and two LayerNorm launches per layer (87 per step with the embedding, the head and
+ * the token bookkeeping). GPT-2-124M shapes only (E 768, 12 layers, 12 heads, vocabulary 50257). */
 
 /* Drop-in for gpt2_decode_step_cuda on the fp16 path: consumes `token` at position `pos` of *kv
  * (kv->len must equal pos), appends every layer's K/V, writes logits[50257] when logits is not NULL
@@ -305,7 +305,7 @@ const char *gpt2_b200_strerror(int code);
  * kernel returned cleanly (the expected result); the device context stays usable. */
 int gpt2_b200_selftest_wait_timeout(unsigned timeout_us);
 
-/* Library version and the number of kernels each entry point launches (for launch accounting). */
+/* Library version string. */
 const char *gpt2_b200_version(void);
 
 #ifdef __cplusplus
