@@ -532,9 +532,10 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
 
 
 # ---------------------------------------------------------------------------------------- CPU legs
-def cpu_reference_sample(seconds: float, max_layers: int | None = None):
-    """Times the reference's own attention() (oracle/_ref, OpenMP over all host threads) on P=1024
-    layers until `seconds` of work (at least 2 layers, at most max_layers)."""
+def cpu_reference_sample(seconds: float, max_layers: int | None = None, p: int = P):
+    """Times the reference's own attention() (oracle/_ref, OpenMP over all host threads) on layers of
+    p rows until `seconds` of work (at least 2 layers, at most max_layers). Reports the median with
+    the min and max over the sampled layers (never a best-of-N)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     try:
@@ -544,7 +545,7 @@ def cpu_reference_sample(seconds: float, max_layers: int | None = None):
         orc, kind = O.Oracle(), "port"
         run = orc.prefill
     threads = O.Oracle().threads()
-    x = O.seeded_qkv(31, P)
+    x = O.seeded_qkv(31, p)
     run(x)  # warm
     times, t_end = [], time.perf_counter() + seconds
     while (len(times) < 2 or time.perf_counter() < t_end) and (max_layers is None or len(times) < max_layers):
@@ -552,8 +553,21 @@ def cpu_reference_sample(seconds: float, max_layers: int | None = None):
         run(x)
         times.append(time.perf_counter() - t0)
     per_layer = statistics.median(times)
-    return {"per_layer_s": per_layer, "layers": len(times), "threads": threads, "kind": kind,
-            "tflops": 2.0 * P * P * E / per_layer / 1e12}
+    return {"P": p, "per_layer_s": per_layer, "min_s": min(times), "max_s": max(times),
+            "layers": len(times), "threads": threads, "nproc": os.cpu_count(), "kind": kind,
+            "tflops": 2.0 * p * p * E / per_layer / 1e12}
+
+
+def cpu_sweep(seconds: float) -> dict:
+    """The reference CPU attention at the other configs[2] prompt lengths (P = 128, 512): per layer
+    median / min / max in ms and the median's TFLOP/s (12 layers cost 12 x one layer on the CPU)."""
+    out = {}
+    for p in (128, 512):
+        c = cpu_reference_sample(seconds, p=p)
+        out[f"P{p}"] = {"layers": c["layers"], "median_ms": c["per_layer_s"] * 1e3,
+                        "min_ms": c["min_s"] * 1e3, "max_ms": c["max_s"] * 1e3,
+                        "tflops": c["tflops"], "kind": c["kind"]}
+    return out
 
 
 def cpu_decode_sample(ctx: int, seconds: float):
@@ -604,14 +618,17 @@ def run_reference(args, rank, world):
     for _ in range(args.warmup):
         for _ in range(layers):
             ref.prefill(x)
-    t0 = time.perf_counter()
+    steps_s = []
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         for _ in range(layers):
             ref.prefill(x)
-    dt = time.perf_counter() - t0
-    ms_step = dt / args.steps * 1e3
-    value = layers * 2.0 * P * P * E / (dt / args.steps) / 1e12
-    sample = f"{layers} of 12 layers (P=1024, fp16-rounded N(0,1) qkv) per step"
+        steps_s.append(time.perf_counter() - t0)
+    step_s = statistics.median(steps_s)
+    ms_step = step_s * 1e3
+    value = layers * 2.0 * P * P * E / step_s / 1e12
+    sample = (f"{layers} of 12 layers (P=1024, fp16-rounded N(0,1) qkv) per step; median of "
+              f"{args.steps} steps, min {min(steps_s) * 1e3:.1f} ms, max {max(steps_s) * 1e3:.1f} ms")
     line = {"impl": "reference", "metric": METRIC,
             "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -619,8 +636,8 @@ def run_reference(args, rank, world):
             "data": "synthetic seeded N(0,1)",
             "config": {"workload": "configs[1] prefill attention, 12 layers, B=1, P=1024, 12x64",
                        "global_batch": 1, "seq_len": P, "parallelism": "host cores"},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-                             "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
+                             "nproc": os.cpu_count(), "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     emit(line)
@@ -744,10 +761,12 @@ def main(argv=None):
         if rank == 0 and world == 1 and "cpu" in legs:
             cpu = cpu_reference_sample(args.cpu_sample_seconds)
             line["cpu_baseline"] = {"value": cpu["tflops"], "unit": "TFLOP/s", "cores": cpu["threads"],
-                                    "kind": cpu["kind"],
+                                    "nproc": cpu["nproc"], "kind": cpu["kind"],
                                     "sample": f"{cpu['layers']} single-layer P=1024 attention calls "
-                                              f"(median {cpu['per_layer_s'] * 1e3:.1f} ms each), "
-                                              "scaled to TFLOP/s"}
+                                              f"(median {cpu['per_layer_s'] * 1e3:.1f} ms each, min "
+                                              f"{cpu['min_s'] * 1e3:.1f}, max {cpu['max_s'] * 1e3:.1f}), "
+                                              "scaled to TFLOP/s",
+                                    "sweep": cpu_sweep(min(1.0, args.cpu_sample_seconds))}
             for c in (128, 512, 1023):
                 key = f"decode_ctx{c}"
                 if key in sec:

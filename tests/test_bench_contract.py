@@ -30,6 +30,7 @@ def test_reference_arm_prints_one_contract_line():
     assert d["metric"] == bench.METRIC and d["unit"] == "TFLOP/s" and d["higher_is_better"] is True
     assert d["value"] > 0 and d["steps"] == 1
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
+    assert d["cpu_baseline"]["nproc"] >= 1
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
@@ -42,3 +43,14 @@ def test_reference_arm_other_ranks_exit_quietly():
                        capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_cpu_baseline_reports_median_min_max_and_the_prompt_sweep():
+    c = bench.cpu_reference_sample(0.0, max_layers=2, p=128)
+    assert c["P"] == 128 and c["layers"] == 2
+    assert c["min_s"] <= c["per_layer_s"] <= c["max_s"] and c["tflops"] > 0
+    assert c["threads"] >= 1 and c["nproc"] >= 1
+    sweep = bench.cpu_sweep(0.0)
+    assert set(sweep) == {"P128", "P512"}
+    for v in sweep.values():
+        assert v["layers"] >= 2 and v["min_ms"] <= v["median_ms"] <= v["max_ms"] and v["tflops"] > 0

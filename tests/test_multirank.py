@@ -56,7 +56,7 @@ def _worker(rank, world, port, out):
 
 def test_max_over_ranks_gloo_two_ranks():
     port = _free_port()
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()  # no fork of a possibly multi-threaded test process
     out = mgr.dict()
     mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
     assert out[0] == out[1] == pytest.approx(32.25)
@@ -83,7 +83,7 @@ def _gather_worker(rank, world, port, out):
 
 def test_token_gather_assembles_sequences_in_order():
     port = _free_port()
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()  # no fork of a possibly multi-threaded test process
     out = mgr.dict()
     mp.spawn(_gather_worker, args=(2, port, out), nprocs=2, join=True)
     want = [[s * 1000 + t for t in range(5)] for s in range(64)]
