@@ -194,7 +194,8 @@ double gpt2_kv_step_bytes_b200(const GPT2KVCache *kv, int len);
 /* Replaces gpt2_kv_append_one (cuda/kvcache.cu:57-64,204-206): writes the K and V parts of qkv[3E]
  * into layer L at position pos, 16-byte vector stores. Legacy default stream. */
 void gpt2_kv_append_one_b200(GPT2KVCache *kv, int L, const gpt2_half *qkv, int pos);
-/* Append for layers L0..L0+nL-1 (rows qkv + l*qkv_layer_stride); position *d_pos if d_pos != NULL. */
+/* Append for layers L0..L0+nL-1 (rows qkv + l*qkv_layer_stride) on `stream`; position *d_pos if
+ * d_pos != NULL (graph replay), else pos. Additive extension of gpt2_kv_append_one. */
 int gpt2_kv_append_b200_stream(GPT2KVCache *kv, int L0, int nL, const gpt2_half *qkv,
                                long long qkv_layer_stride, const int *d_pos, int pos,
                                cudaStream_t stream);
