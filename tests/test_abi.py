@@ -152,6 +152,45 @@ def test_decode_rejects_bad_arguments(lib):
     assert lib.gpt2_b200_last_error() == G.EINVAL
 
 
+def test_layer_batched_and_fixed_scratch_decode_reject_bad_arguments(lib):
+    """The multi-layer, batched and no-allocation decode entry points refuse bad arguments before any
+    CUDA call. Only refused cases appear here: a valid call would launch on these fake pointers."""
+    kv = G.cache_view(4096, 12, 1024)
+    ref = ctypes.byref(kv)
+    layers = lib.gpt2_attn_decode_b200_layers
+    assert layers(16, 768, 16, 2304, ref, 11, 2, None, 5, 0, None) == G.EINVAL   # layers 11..12
+    assert layers(16, 769, 16, 2304, ref, 0, 2, None, 5, 0, None) == G.EINVAL    # stride % 8
+    assert layers(16, 768, 16, 2304, ref, 0, 2, None, 0, 0, None) == G.EINVAL    # len 0
+    assert layers(16, 768, 16, 2304, ref, 0, 2, None, 5, 1025, None) == G.EINVAL  # max_len > maxT
+    assert layers(16, 768, 16, 2304, ref, 0, 2, None, 9, 8, None) == G.EINVAL    # len > max_len
+    batched = lib.gpt2_attn_decode_b200_batched
+    assert batched(16, 768, 16, 2304, 16, 16, 16, 0, 12, 1024, 0, None) == G.EINVAL  # B = 0
+    assert batched(16, 770, 16, 2304, 16, 16, 16, 4, 12, 1024, 0, None) == G.EINVAL  # stride % 8
+    assert batched(16, 768, 16, 2304, 16, 16, 16, 4, 12, 1024, 2048, None) == G.EINVAL  # max_len
+    assert batched(16, 768, 16, 2304, None, 16, 16, 4, 12, 1024, 0, None) == G.EINVAL  # no slabs
+    noalloc = lib.gpt2_attn_decode_b200_layers_noalloc
+    assert noalloc(16, 768, 16, 2304, ref, 0, 12, 0, None) == G.EINVAL     # len 0
+    assert noalloc(16, 768, 16, 2304, ref, 0, 12, 1025, None) == G.EINVAL  # len > maxT
+    assert noalloc(18, 768, 16, 2304, ref, 0, 12, 5, None) == G.EINVAL     # misaligned att
+    wide = G.cache_view(4096, 12, 1024, n_head=200)  # 2400 (layer, head) pairs > 2048
+    assert noalloc(16, 12800, 16, 38400, ctypes.byref(wide), 0, 12, 5, None) == G.EINVAL
+    long_ = G.cache_view(4096, 12, 4096)  # 144 pairs x 32 splits of 128 keys > 1985 partials
+    assert noalloc(16, 768, 16, 2304, ctypes.byref(long_), 0, 12, 4096, None) == G.EINVAL
+
+
+def test_prefill_with_cache_fill_rejects_a_mismatched_cache(lib):
+    kv = G.cache_view(4096, 12, 64)
+    ref = ctypes.byref(kv)
+    fill = lib.gpt2_attention_kv_b200_stream
+    assert fill(16, 16, ref, 0, 65, 768, 12, 64, None) == G.EINVAL   # T > maxT
+    assert fill(16, 16, ref, 12, 8, 768, 12, 64, None) == G.EINVAL   # layer out of range
+    other = G.cache_view(4096, 12, 64, n_head=6)
+    assert fill(16, 16, ctypes.byref(other), 0, 8, 768, 12, 64, None) == G.EINVAL  # nHead != H
+    assert fill(16, 16, None, 0, 8, 768, 12, 64, None) == G.EINVAL
+    lib.gpt2_attention_kv_b200(16, 16, ref, 0, 65, 768, 12, 64)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+
+
 def test_model_entry_points_reject_bad_arguments(lib):
     """The decode-step and linear-layer entry points refuse bad arguments before any CUDA call."""
     w = G.GPT2WeightsGPU()  # every pointer NULL
