@@ -191,6 +191,21 @@ def test_prefill_with_cache_fill_rejects_a_mismatched_cache(lib):
     assert lib.gpt2_b200_last_error() == G.EINVAL
 
 
+def test_step_attention_reserve_and_gemv_reject_bad_arguments(lib):
+    kv = G.cache_view(4096, 12, 64)
+    ref = ctypes.byref(kv)
+    step = lib.gpt2_b200_decode_attn_step
+    assert step(16, 768, 18, 2304, ref, None, 3, None) == G.EINVAL   # misaligned qkv
+    assert step(16, 768, 16, 2301, ref, None, 3, None) == G.EINVAL   # qkv stride % 8
+    assert step(16, 768, 16, 2304, ref, None, 64, None) == G.EINVAL  # pos >= maxT
+    assert step(16, 765, 16, 2304, ref, None, 3, None) == G.EINVAL   # att stride % 8
+    assert step(16, 768, 16, 2304, None, None, 3, None) == G.EINVAL
+    for args in ((0, 12, 1024), (1, 0, 1024), (1, 12, 0)):
+        assert lib.gpt2_b200_reserve(*args) == G.EINVAL
+    lib.gpt2_gemv_b200(None, 16, 16, None, 768, 768)
+    assert lib.gpt2_b200_last_error() == G.EINVAL
+
+
 def test_model_entry_points_reject_bad_arguments(lib):
     """The decode-step and linear-layer entry points refuse bad arguments before any CUDA call."""
     w = G.GPT2WeightsGPU()  # every pointer NULL
