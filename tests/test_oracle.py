@@ -37,6 +37,15 @@ def test_golden_config1_T128_bit_exact(oracle):
     assert np.array_equal(oracle.prefill(qkv), g["att"])
 
 
+def test_golden_fixtures_reproduced_by_the_reference():
+    """The committed fixtures are what the reference's own compiled attention() returns today."""
+    ref = _ref_cpu()
+    g = np.load(os.path.join(GOLD, "prefill_T40.npz"))
+    assert np.array_equal(ref.prefill(g["qkv_f16"].view(np.float16).astype(np.float32)), g["att"])
+    g = np.load(os.path.join(GOLD, "prefill_T128_cfg1.npz"))
+    assert np.array_equal(ref.prefill(O.seeded_qkv(int(g["seed"]), int(g["T"]))), g["att"])
+
+
 @pytest.mark.parametrize("T", [1, 2, 31, 32, 33, 127, 128, 129, 161, 300])
 def test_oracle_equals_reference_cpu(oracle, T):
     ref = _ref_cpu()
