@@ -626,7 +626,7 @@ def run_reference(args, rank, world):
         steps_s.append(time.perf_counter() - t0)
     step_s = statistics.median(steps_s)
     ms_step = step_s * 1e3
-    value = layers * 2.0 * P * P * E / step_s / 1e12
+    value = prefill_flops(P, layers) / step_s / 1e12
     sample = (f"{layers} of 12 layers (P=1024, fp16-rounded N(0,1) qkv) per step; median of "
               f"{args.steps} steps, min {min(steps_s) * 1e3:.1f} ms, max {max(steps_s) * 1e3:.1f} ms")
     line = {"impl": "reference", "metric": METRIC,

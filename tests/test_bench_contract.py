@@ -54,3 +54,17 @@ def test_cpu_baseline_reports_median_min_max_and_the_prompt_sweep():
     assert set(sweep) == {"P128", "P512"}
     for v in sweep.values():
         assert v["layers"] >= 2 and v["min_ms"] <= v["median_ms"] <= v["max_ms"] and v["tflops"] > 0
+
+
+def test_algorithmic_work_conventions(lib):
+    """The roofline numerators: prefill FLOPs 2*P^2*768 per layer (4*P^2*64*12/2), decode bytes
+    2*L*H*len*64*2, the latter equal to the library's gpt2_kv_step_bytes (the reference's formula)."""
+    import ctypes
+
+    import gpt2_b200 as G
+    assert bench.prefill_flops(128, 1) == 25165824.0
+    assert bench.prefill_flops(1024, 1) == 1610612736.0
+    assert bench.prefill_flops(1024) == 19327352832.0  # the headline launch: 19.33 GFLOP
+    kv = G.cache_view(4096, 12, 1024)
+    for n in (128, 512, 1023):
+        assert bench.decode_bytes(n) == 36864.0 * n == lib.gpt2_kv_step_bytes_b200(ctypes.byref(kv), n)
