@@ -71,9 +71,13 @@ int kv_alloc(GPT2KVCache *kv, int nLayer, int nHead, int headDim, int maxT) {
     kv->bytes = static_cast<size_t>(2) * nLayer * nHead * maxT * headDim * sizeof(__half);
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return 1;
-    if (kv->bytes + (static_cast<size_t>(64) << 20) > free_b) {  // same 64 MiB headroom rule
-        fprintf(stderr, "[kv-b200] plan needs %.1f MB but only %.1f MB free -> refusing to allocate\n",
-                kv->bytes / 1e6, free_b / 1e6);
+    // The reference's refusal rule: the arena must leave at least 64 MiB of device memory free.
+    const size_t headroom = static_cast<size_t>(64) << 20;
+    if (kv->bytes + headroom > free_b) {
+        fprintf(stderr,
+                "[gpt2_b200] KV cache of %zu bytes not allocated: %zu bytes free on the device, and "
+                "%zu must stay free after it\n",
+                kv->bytes, free_b, headroom);
         return 1;
     }
     void *p = nullptr;

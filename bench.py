@@ -54,6 +54,18 @@ def decode_bytes(length: int, layers: int = LAYERS) -> float:
 
 
 # ---------------------------------------------------------------------------------------- helpers
+def r4(x):
+    """A float to 4 significant digits (keeps the one-line summary short); None passes through."""
+    return None if x is None else float(f"{x:.4g}")
+
+
+def workload_config(world: int) -> dict:
+    """The `config` of both arms' JSON lines (identical, so the two lines compare like for like)."""
+    return {"workload": "configs[1] prefill attention, 12 layers x B=1 x P=1024, 12 heads x 64",
+            "global_batch": world, "seq_len": P, "layers": LAYERS, "parallelism": f"seq-shard x{world}",
+            "l2": "GPU arm: inputs rotate over sets totalling > 2x the 126 MB L2"}
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -108,18 +120,45 @@ def max_over_ranks(value: float, world: int) -> float:
     return float(t.item())
 
 
-def gather_shards(out, shard, world: int) -> None:
-    """Every rank's equal-sized shard (rank order = shard_range order) into `out` on every rank: one
-    NCCL all-gather into device memory (over NVLink between the GPUs of a box); gloo (CPU tests)
-    gathers a list and concatenates."""
-    import torch
-    import torch.distributed as dist
-    if dist.get_backend() == "nccl":
-        dist.all_gather_into_tensor(out, shard)
-    else:
-        parts = [torch.empty_like(shard) for _ in range(world)]
-        dist.all_gather(parts, shard)
-        out.copy_(torch.cat(parts, dim=0))
+class HostGather:
+    """Host-side gather of every rank's output rows into ONE host buffer, with no collective: the
+    buffer is a file in /dev/shm that every rank of the box maps; each rank page-locks its mapping
+    (cudaHostRegister) and copies its rows [lo, hi) device -> host straight into their place. The
+    ranks of one job share a name derived from the launcher's process id and the rendezvous port.
+
+    Protocol: construct on every rank (rank 0 makes the file, a barrier, every rank maps it), then
+    rows(lo, hi) is this rank's slice, then close() on every rank (a barrier before rank 0 removes
+    the file; the mappings stay valid until their last view is dropped). Without CUDA (gloo tests)
+    the mapping is used unregistered."""
+
+    def __init__(self, shape, dtype, rank: int, world: int, tag: str = "tokens"):
+        import torch
+        self.rank, self.world = rank, world
+        key = f"{os.getppid()}_{os.environ.get('MASTER_PORT', '0')}_{tag}"
+        self.path = f"/dev/shm/gpt2b200_gather_{key}"
+        nbytes = int(np.prod(shape)) * np.dtype(dtype).itemsize
+        if rank == 0:
+            with open(self.path, "wb") as f:
+                f.truncate(nbytes)
+        barrier(world)
+        self.array = np.memmap(self.path, dtype=dtype, mode="r+", shape=tuple(shape))
+        self.tensor = torch.from_numpy(self.array)
+        self.registered = False
+        if torch.cuda.is_available():
+            rc = torch.cuda.cudart().cudaHostRegister(self.tensor.data_ptr(), nbytes, 0)
+            self.registered = int(rc) == 0
+
+    def rows(self, lo: int, hi: int):
+        return self.tensor[lo:hi]
+
+    def close(self) -> None:
+        import torch
+        if self.registered:
+            torch.cuda.cudart().cudaHostUnregister(self.tensor.data_ptr())
+            self.registered = False
+        barrier(self.world)  # every rank has finished with the file
+        if self.rank == 0:
+            os.unlink(self.path)
 
 
 def barrier(world: int) -> None:
@@ -465,11 +504,10 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
               "gpt2_b200_batch_create")
     h_prompt = torch.from_numpy(prompt_all[lo:hi].copy()).pin_memory()
     h_plen = torch.from_numpy(plen_all[lo:hi].copy()).pin_memory()
-    # Multi-GPU: every rank's tokens are gathered over NVLink into rank 0's memory (NCCL all-gather,
-    # equal shards), then copied to the host once; with one GPU the tokens go straight to the host.
-    gather = world > 1 and total_seqs % world == 0
-    d_all = torch.empty((total_seqs, n_steps + 1), dtype=torch.int32, device="cuda") if gather else None
-    h_out = torch.empty((total_seqs if gather else B, n_steps + 1), dtype=torch.int32).pin_memory()
+    # Every rank copies its sequences' tokens device -> host into its rows of one page-locked host
+    # buffer shared by all ranks (no collective; with one GPU the buffer is this process's own).
+    gather = HostGather((total_seqs, n_steps + 1), np.int32, rank, world)
+    h_out = gather.rows(lo, hi)
     d_prompt = torch.empty((B, 512), dtype=torch.int32, device="cuda")
     d_plen = torch.empty(B, dtype=torch.int32, device="cuda")
     d_out = torch.empty((B, n_steps + 1), dtype=torch.int32, device="cuda")
@@ -481,12 +519,7 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
         lib.check(lib.gpt2_b200_batch_generate(h, d_prompt.data_ptr(), 512, d_plen.data_ptr(), n_steps,
                                                d_out.data_ptr(), n_steps + 1, flags, stream.cuda_stream),
                   "gpt2_b200_batch_generate")
-        if gather:
-            gather_shards(d_all, d_out, world)
-            if rank == 0:
-                h_out.copy_(d_all, non_blocking=True)
-        else:
-            h_out.copy_(d_out, non_blocking=True)
+        h_out.copy_(d_out, non_blocking=gather.registered)
 
     def timed(flags):
         run(flags)  # warm-up (the first call also captures the step's graph)
@@ -501,17 +534,15 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
         return max_over_ranks(s.elapsed_time(e), world)
 
     ms = timed(0)
-    tokens = h_out.numpy().copy()
+    barrier(world)  # every rank's rows of the shared host buffer are written
+    tokens = np.array(gather.array)  # all sequences, in global order
     ms_attn = timed(G.GEN_ATTENTION_ONLY)
     launches = lib.gpt2_b200_batch_launches_per_step(h, 0)
     lib.gpt2_b200_batch_destroy(h)
     status = lib.status()
-    if gather:  # rank 0 holds every sequence's tokens
-        rows, first = (range(total_seqs), 0) if rank == 0 else (range(0), 0)
-    else:
-        rows, first = range(B), lo
-    prompts_kept = all(np.array_equal(tokens[r, :plen_all[first + r]], prompt_all[first + r, :plen_all[first + r]])
-                       for r in rows)
+    gather.close()
+    rows = range(total_seqs) if rank == 0 else range(lo, hi)  # rank 0 checks the whole gather
+    prompts_kept = all(np.array_equal(tokens[r, :plen_all[r]], prompt_all[r, :plen_all[r]]) for r in rows)
     # Tokens the model produced (all ranks): the step at position t emits the token of t+1, which is
     # generated once t+1 >= the prompt length.
     generated = int((n_steps + 1 - plen_all).clip(min=0).sum())
@@ -527,8 +558,9 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
             "hbm_gbs_per_gpu": (n_steps * w_bytes + kv_bytes) / (ms * 1e-3) / 1e9,
             "prompts_kept": bool(prompts_kept), "status": status, "launches_per_step": launches,
             "h2d_bytes": int(h_prompt.numel() * 4 + h_plen.numel() * 4),
-            "d2h_bytes": int(h_out.numel() * 4) if (rank == 0 or not gather) else 0,
-            "output_gather": "NCCL all-gather over NVLink to rank 0, one D2H" if gather else "D2H per rank"}
+            "d2h_bytes": int(h_out.numel() * 4),
+            "output_gather": "each rank D2H into its rows of one shared page-locked host buffer"
+                             + ("" if gather.registered else " (unregistered)")}
 
 
 # ---------------------------------------------------------------------------------------- CPU legs
@@ -633,9 +665,8 @@ def run_reference(args, rank, world):
             "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate over fp32",
-            "data": "synthetic seeded N(0,1)",
-            "config": {"workload": "configs[1] prefill attention, 12 layers, B=1, P=1024, 12x64",
-                       "global_batch": 1, "seq_len": P, "parallelism": "host cores"},
+            "data": "synthetic seeded N(0,1) fp16 qkv (no dataset)",
+            "config": workload_config(world),
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
                              "nproc": os.cpu_count(), "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -692,38 +723,46 @@ def main(argv=None):
 
     line = {
         "metric": METRIC,
-        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": region / args.steps, "higher_is_better": True,
+        "value": r4(value), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r4(region / args.steps), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
-        "data": "synthetic: seeded N(0,1) fp16 qkv per layer (no dataset involved)",
-        "config": {"workload": "configs[1] prefill attention, 12 layers x B=1 x P=1024, 12 heads x 64, "
-                               "one batched launch per step",
-                   "global_batch": world, "seq_len": P, "layers": LAYERS, "parallelism": f"seq-shard x{world}",
-                   "l2": f"{pre['rotating_sets']} rotating input sets of {pre['set_bytes'] / 1e6:.1f} MB "
-                         f"(> 126 MB L2 in total)",
-                   "timing": "one CUDA event pair around the K back-to-back steps; the stream is held by a "
-                             "fixed-cycle busy kernel before the start event while the host queues them",
-                   "host_kept_ahead": pre["host_kept_ahead"]},
+        "data": "synthetic seeded N(0,1) fp16 qkv (no dataset)",
+        "config": workload_config(world),
         "gpu_launches": pre["launches"],
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "peak_source": f"{peak_src} dense bf16/fp16 burst (MEASURED_PEAKS.json bf16_tflops)",
-                     "traffic": traffic, "kernel": "k_flash_prefill_tc",
-                     "algorithmic_flops_per_launch": flops_step},
-        "clocks": clocks.summary(),
+        "roofline": {"bound": "tensor", "achieved": r4(achieved), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": r4(achieved / peaks["bf16_tflops"]),
+                     "traffic": traffic, "peak_source": peak_src},
+        "clocks": {k: v for k, v in clocks.summary().items() if k != "samples"},
     }
+    # Everything measured, including what the one-line summary leaves out, goes to standard error
+    # as a second JSON object (the stdout line is kept short enough to be read whole).
+    details = {"prefill": pre, "clocks": clocks.summary(), "peak_source": peak_src,
+               "timing": "one CUDA event pair around the K back-to-back steps; the stream is held by a "
+                         "fixed-cycle busy kernel before the start event while the host queues them"}
 
     legs = set(args.legs.split(",")) if args.legs != "all" else {
         "decode", "decode_b64", "per_layer", "batched", "model_decode", "e2e", "cpu"}
     if not args.no_secondary:
         sec = {}
         try:
+            if "e2e" in legs:
+                e2e = bench_e2e_prefill(torch, lib, min(args.steps, 30), args.warmup, seed=1300 + rank)
+                e2e_ms = max_over_ranks(e2e["ms_per_step"], world)
+                line["e2e"] = {"value": r4(world * flops_step / (e2e_ms * 1e-3) / 1e12), "unit": "TFLOP/s",
+                               "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]}
+                sec["e2e"] = dict(e2e, ms_per_step=e2e_ms,
+                                  path="per layer: pinned host qkv -> cudaMemcpyAsync -> "
+                                       "gpt2_attention_b200_stream (the reference's attention slot) -> att "
+                                       f"to pinned host, {e2e['streams']} streams overlapping upload, "
+                                       "attention and download")
             if "decode" in legs:
                 dec = bench_decode(torch, lib, G, min(args.steps, 400), args.warmup, CTX, seed=500 + rank)
-                dec["roofline"] = {"bound": "hbm", "achieved": dec["kv_gbs"], "peak": peaks["hbm_gbs"],
-                                   "unit": "GB/s", "frac": dec["kv_gbs"] / peaks["hbm_gbs"],
-                                   "traffic": profile_traffic("decode_stream_ctx1023_L12"),
-                                   "kernel": "k_decode_stream"}
+                dtraffic = profile_traffic("decode_stream_ctx1023_L12")
+                line["decode_kv_gbs_ctx1023"] = r4(dec["kv_gbs"])
+                line["decode_us_per_step_ctx1023"] = r4(dec["us_per_step"])
+                line["decode_roofline"] = {"bound": "hbm", "achieved": r4(dec["kv_gbs"]),
+                                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                           "frac": r4(dec["kv_gbs"] / peaks["hbm_gbs"]), "traffic": dtraffic}
                 sec["decode_ctx1023"] = dec
                 for c in (128, 512):
                     d = bench_decode(torch, lib, G, min(args.steps, 200), args.warmup, c, seed=700 + rank)
@@ -731,48 +770,46 @@ def main(argv=None):
             if "decode_b64" in legs:
                 for c in (512, 1023):
                     d = bench_decode_batched(torch, lib, 20, args.warmup, world, rank, c, seed=800 + rank)
-                    d["roofline"] = {"bound": "hbm", "achieved": d["kv_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
-                                     "unit": "GB/s", "frac": d["kv_gbs_per_gpu"] / peaks["hbm_gbs"],
-                                     "kernel": "k_decode_stream<4, 3>"}
+                    d["frac"] = d["kv_gbs_per_gpu"] / peaks["hbm_gbs"]
                     sec[f"decode_B64_ctx{c}"] = d
+                line["decode_b64_kv_gbs_ctx1023"] = r4(sec["decode_B64_ctx1023"]["kv_gbs_per_gpu"])
             if "per_layer" in legs:
-                sec["prefill_per_layer_launches"] = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
+                pl = bench_prefill_per_layer(torch, lib, 50, args.warmup, 900 + rank)
+                sec["prefill_per_layer_launches"] = pl
+                line["prefill_per_layer_tflops"] = r4(pl["tflops"])
             if "batched" in legs:
-                sec["batched_B64"] = bench_batched(torch, lib, 3, args.warmup, world, rank, seed=1200 + rank)
+                bt = bench_batched(torch, lib, 3, args.warmup, world, rank, seed=1200 + rank)
+                sec["batched_B64"] = bt
+                line["batched_b64_tflops"] = r4(bt["aggregate_tflops"])
             if "model_decode" in legs:
                 md = bench_model_decode(torch, lib, G, world, rank, seed=4242, ctx=args.model_steps)
-                md["roofline"] = {"bound": "hbm", "achieved": md["hbm_gbs_per_gpu"], "peak": peaks["hbm_gbs"],
-                                  "unit": "GB/s", "frac": md["hbm_gbs_per_gpu"] / peaks["hbm_gbs"],
-                                  "bytes": "weights once per step + every sequence's K/V over its context"}
+                md["frac"] = md["hbm_gbs_per_gpu"] / peaks["hbm_gbs"]
                 sec["model_decode_B64"] = md
-                line["decode_tok_per_s"] = md["tok_per_s"]
-            if "e2e" in legs:
-                e2e = bench_e2e_prefill(torch, lib, min(args.steps, 30), args.warmup, seed=1300 + rank)
-                e2e_ms = max_over_ranks(e2e["ms_per_step"], world)
-                line["e2e"] = {"value": world * flops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                               "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                               "ms_per_step": e2e_ms, "host_kept_ahead": e2e["host_kept_ahead"],
-                               "path": "per layer: pinned host qkv -> cudaMemcpyAsync -> gpt2_attention_b200_stream "
-                                       f"(the reference's attention slot) -> att to pinned host, {e2e['streams']} "
-                                       "streams overlapping upload, attention and download"}
+                line["decode_tok_per_s"] = r4(md["tok_per_s"])
+                line["decode_attention_share"] = r4(md["attention_share"])
         except Exception as ex:  # noqa: BLE001 - the headline stands; the failure is reported
             sec["error"] = repr(ex)
-        line["secondary"] = sec
+            line["secondary_error"] = repr(ex)[:200]
+        details["secondary"] = sec
         if rank == 0 and world == 1 and "cpu" in legs:
             cpu = cpu_reference_sample(args.cpu_sample_seconds)
-            line["cpu_baseline"] = {"value": cpu["tflops"], "unit": "TFLOP/s", "cores": cpu["threads"],
-                                    "nproc": cpu["nproc"], "kind": cpu["kind"],
-                                    "sample": f"{cpu['layers']} single-layer P=1024 attention calls "
-                                              f"(median {cpu['per_layer_s'] * 1e3:.1f} ms each, min "
-                                              f"{cpu['min_s'] * 1e3:.1f}, max {cpu['max_s'] * 1e3:.1f}), "
-                                              "scaled to TFLOP/s",
-                                    "sweep": cpu_sweep(min(1.0, args.cpu_sample_seconds))}
+            line["cpu_baseline"] = {"value": r4(cpu["tflops"]), "unit": "TFLOP/s", "cores": cpu["threads"],
+                                    "kind": cpu["kind"],
+                                    "sample": f"{cpu['layers']} P=1024 layers, median "
+                                              f"{cpu['per_layer_s'] * 1e3:.1f} ms (min {cpu['min_s'] * 1e3:.1f}, "
+                                              f"max {cpu['max_s'] * 1e3:.1f})"}
+            details["cpu_baseline"] = dict(cpu, sweep=cpu_sweep(min(1.0, args.cpu_sample_seconds)))
             for c in (128, 512, 1023):
                 key = f"decode_ctx{c}"
                 if key in sec:
-                    sec[key]["cpu_baseline"] = cpu_decode_sample(c, 1.0)
+                    cd = cpu_decode_sample(c, 1.0)
+                    sec[key]["cpu_baseline"] = cd
+                    if c == CTX:
+                        line["decode_cpu_baseline"] = {"value": r4(cd["value"]), "unit": "GB/s",
+                                                       "cores": cd["cores"], "kind": cd["kind"]}
     if rank == 0:
         emit(line)
+        sys.stderr.write("bench details: " + json.dumps(details, default=str) + "\n")
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

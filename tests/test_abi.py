@@ -10,6 +10,8 @@ import pytest
 import gpt2_b200 as G
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# The reference tree (build container only): $GPT2_REFERENCE_DIR, else `reference` beside this repo.
+REF_DIR = os.environ.get("GPT2_REFERENCE_DIR", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def test_library_exports_every_declared_function(lib):
@@ -70,7 +72,7 @@ int main(void) {
     assert vals[0] == ctypes.sizeof(G.GPT2LayerGPU) and vals[2] == ctypes.sizeof(G.GPT2WeightsGPU)
 
 
-@pytest.mark.skipif(not os.path.isdir("/root/reference/cuda"), reason="reference tree not present")
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF_DIR, "cuda")), reason="reference tree not present")
 def test_header_compiles_after_the_reference_headers():
     """A reference translation unit includes its own kernels.cuh / kvcache.cuh first, then this
     header, and calls the drop-ins with the reference's own types (compile only)."""
@@ -92,7 +94,7 @@ void harness(const GPT2WeightsGPU *w, GPT2KVCache *kv, GPT2ScratchGPU *s, half *
 }
 ''')
     subprocess.run(["nvcc", "-std=c++17", "-c", "-o", os.path.join(d, "harness.o"),
-                    "-I", "/root/reference/cuda", "-I", "/root/reference/model",
+                    "-I", os.path.join(REF_DIR, "cuda"), "-I", os.path.join(REF_DIR, "model"),
                     "-I", os.path.join(ROOT, "include"), cu], check=True, capture_output=True)
 
 

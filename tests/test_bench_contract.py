@@ -27,6 +27,8 @@ def test_reference_arm_prints_one_contract_line():
               "cpu_baseline", "e2e"):
         assert k in d, k
     assert d["impl"] == "reference"
+    assert d["config"] == bench.workload_config(1)  # the b200 arm prints the same dict
+    assert len(lines[0]) < 1400  # read whole from the tail of the run's output
     assert d["metric"] == bench.METRIC and d["unit"] == "TFLOP/s" and d["higher_is_better"] is True
     assert d["value"] > 0 and d["steps"] == 1
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1

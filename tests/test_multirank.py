@@ -1,9 +1,10 @@
 """Multi-rank host logic on CPU (gloo, world size 2): sequence sharding has no collective on the data
-path; the only collectives are the barrier, the MAX all-reduce of per-rank timings, and
-the gather of every rank's generated tokens into rank order."""
+path; the only collectives are the barrier and the MAX all-reduce of per-rank timings. configs[4]'s
+generated tokens are gathered on the host: every rank copies its rows into one shared host buffer."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
@@ -75,16 +76,20 @@ def _gather_worker(rank, world, port, out):
     # each rank's "generated tokens": row = global sequence index * 1000 + position
     shard = torch.tensor([[(lo + b) * 1000 + t for t in range(steps)] for b in range(hi - lo)],
                          dtype=torch.int32)
-    full = torch.empty((total, steps), dtype=torch.int32)
-    bench.gather_shards(full, shard, world)
-    out[rank] = full.tolist()
-    dist.destroy_process_group()
+    g = bench.HostGather((total, steps), np.int32, rank, world)
+    g.rows(lo, hi).copy_(shard)  # this rank's rows only, no collective
+    bench.barrier(world)
+    out[rank] = np.array(g.array).tolist()
+    path = g.path
+    g.close()
+    out[f"gone{rank}"] = not os.path.exists(path) if rank == 0 else True
 
 
-def test_token_gather_assembles_sequences_in_order():
+def test_host_gather_assembles_sequences_in_order_without_a_collective():
     port = _free_port()
     mgr = mp.get_context("spawn").Manager()  # no fork of a possibly multi-threaded test process
     out = mgr.dict()
     mp.spawn(_gather_worker, args=(2, port, out), nprocs=2, join=True)
     want = [[s * 1000 + t for t in range(5)] for s in range(64)]
     assert out[0] == want and out[1] == want
+    assert out["gone0"]  # the shared file is removed once every rank has closed it
