@@ -28,6 +28,7 @@ int kv_alloc(GPT2KVCache *kv, int nLayer, int nHead, int headDim, int maxT);
 int launch_kv_append(GPT2KVCache *kv, int L0, int nL, const __half *qkv, long long qkv_stride,
                      const int *d_pos, int pos, cudaStream_t stream);
 int launch_kv_scatter(GPT2KVCache *kv, int L, const __half *qkv, int T, cudaStream_t stream);
+unsigned noalloc_status(bool clear);
 
 namespace {
 constexpr int kMaxDevices = 64;
@@ -291,6 +292,7 @@ unsigned gpt2_b200_status(int clear) {
     unsigned v = 0;
     if (cudaMemcpy(&v, ctx->status, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
         return 0xFFFFFFFFu;
+    v |= noalloc_status(clear != 0);  // the no-allocation decode keeps its word in its fixed scratch
     if (clear && v) {
         cudaMemset(ctx->status, 0, sizeof(unsigned));
         // A kernel that gave up may have left split-merge arrival counters part-way: re-arm them.

@@ -321,7 +321,9 @@ std::mutex g_mu;
 unsigned *g_addr[kMaxDevices] = {};
 
 // Looks up the device address of g_scratch for the current device, once per device. (In host code
-// the name g_scratch is only a host-side stand-in; passing it to a kernel would be wrong.)
+// the name g_scratch is only a host-side stand-in; passing it to a kernel would be wrong.) The
+// address is kept for the life of the process: after cudaDeviceReset, which unloads the library's
+// module, it is stale and the entry point must not be called again.
 unsigned *scratch_address(int *rc) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
@@ -343,14 +345,38 @@ unsigned *scratch_address(int *rc) {
 }
 
 }  // namespace noalloc
+
+// The status word inside the fixed scratch of the current device (0 when the no-allocation entry
+// point has not run there), cleared when `clear`; gpt2_b200_status() ORs it into what it reports.
+// The caller has synchronised the device.
+unsigned noalloc_status(bool clear) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= noalloc::kMaxDevices) return 0;
+    unsigned *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(noalloc::g_mu);
+        base = noalloc::g_addr[dev];
+    }
+    if (!base) return 0;
+    unsigned *status = base + noalloc::NOALLOC_COUNTERS;
+    unsigned v = 0;
+    if (cudaMemcpy(&v, status, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear && v) cudaMemset(status, 0, sizeof(unsigned));
+    return v;
+}
+
 }  // namespace b200
 
-// Same computation and output as gpt2_attn_decode_b200_layers with a host length, but it allocates
-// nothing: the scratch is the fixed array above. The first call on each device looks up that
-// array's device address (make that first call before any stream capture). Every call on a device
+// Same computation as gpt2_attn_decode_b200_layers with a host length, run by k_decode_split (an
+// 8-threads-per-key split-context kernel with a last-CTA merge; the regular entry point runs
+// k_decode_stream), but it allocates nothing: the scratch is the fixed array above. The first call
+// on each device looks up that array's device address; with CUDA's lazy module loading that is also
+// when the driver places the library module's globals, this array among them, in device memory.
+// So make the first call on each device during initialisation: before a pool allocator takes the
+// rest of HBM or allocations are frozen, and before any stream capture. Every call on a device
 // shares the one array and leaves its contents behind; the arrival counters are cleared at the
 // start of each call, so calls must not overlap on the GPU (issue them on one stream, or order
-// them), or they race on the shared scratch.
+// them), or they race on the shared scratch. Its status word is reported by gpt2_b200_status().
 extern "C" int gpt2_attn_decode_b200_layers_noalloc(gpt2_half *att, long long att_layer_stride,
                                                     const gpt2_half *q, long long q_layer_stride,
                                                     const GPT2KVCache *kv, int L0, int nL, int len,

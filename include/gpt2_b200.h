@@ -151,11 +151,16 @@ int gpt2_attn_decode_b200_layers(gpt2_half *att, long long att_layer_stride, con
  * allocate device memory (a pool allocator that owns all of HBM, a host that freezes allocations
  * after start-up, a latency-critical loop that cannot absorb a synchronising cudaMalloc). No
  * counterpart in the reference. It allocates nothing: its scratch is a fixed ~520 KiB array inside
- * the library image, one per GPU, held until the process exits. Limits: nL * nHead <= 2048 and
+ * the library image, one per GPU, held until the process exits. It runs k_decode_split (8 threads per
+ * key row, split partials merged by the last CTA), not the regular entry point's k_decode_stream;
+ * results agree within the library's parity tolerance. Limits: nL * nHead <= 2048 and
  * nL * nHead * ceil(len / 128) <= 1985 (all 12 GPT-2 layers up to 1024 keys); larger requests
  * return GPT2_B200_EINVAL before launching. The first call on a device looks up the array's device
- * address, so make it before any stream capture. All calls on a device share the array (its counters
- * are cleared at the start of each call): calls that overlap on the GPU race, so keep them ordered. */
+ * address, and under CUDA's lazy module loading that is when the driver places the array in device
+ * memory: make the first call on each device during initialisation, before allocations are frozen
+ * and before any stream capture. Not valid after cudaDeviceReset. All calls on a device share the
+ * array (its counters are cleared at the start of each call): calls that overlap on the GPU race,
+ * so keep them ordered. Its status bits are reported by gpt2_b200_status(). */
 int gpt2_attn_decode_b200_layers_noalloc(gpt2_half *att, long long att_layer_stride,
                                          const gpt2_half *q, long long q_layer_stride,
                                          const GPT2KVCache *kv, int L0, int nL, int len,

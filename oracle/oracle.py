@@ -187,6 +187,7 @@ class RefGPU:
             "ref_gpu_kv_append_one": [vp, ci, ci, vp, ci],
             "ref_gpu_kv_scatter_prefill": [vp, ci, ci, vp, ci],
             "ref_gpu_decode_step": [vp, vp, ci, ci, ci, vp, vp],
+            "ref_gpu_prefill_fill_cache": [vp, vp, ci, vp, ci],
         }.items():
             fn = getattr(lib, name)
             fn.argtypes = args
@@ -216,6 +217,10 @@ class RefGPU:
         self._ok(self.lib.ref_gpu_kv_scatter_prefill(kv_ptr, max_t, layer, qkv_ptr, t),
                  "ref scatter")
 
+    def prefill_fill_cache(self, weights_ptr: int, kv_ptr: int, max_t: int, ids_ptr: int, t: int) -> None:
+        """The reference's gpt2_prefill_fill_cache for one sequence: rows 0..t-1 of every layer."""
+        self._ok(self.lib.ref_gpu_prefill_fill_cache(weights_ptr, kv_ptr, max_t, ids_ptr, t),
+                 "ref prefill fill cache")
 
     def decode_step(self, weights_ptr: int, kv_ptr: int, max_t: int, token: int, pos: int,
                     logits_ptr: int | None, caps_ptr: int | None = None) -> None:

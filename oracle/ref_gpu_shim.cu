@@ -13,6 +13,7 @@
 //   gpt2_kv_scatter_prefill    cuda/kvcache.cu:78-81
 //   gpt2_decode_step_cuda      cuda/kvcache.cu:233-269 with GPT2_BACKEND_GEMV (kvcache.cu:280-290),
 //                              the reference's fp16 decode path (M=1 GEMVs + its attention)
+//   gpt2_prefill_fill_cache    cuda/kvcache.cu:271-277 (the prefill forward that fills the cache)
 #include "kernels.cuh"
 #include "kvcache.cuh"
 #include <cuda_runtime.h>
@@ -74,6 +75,25 @@ int ref_gpu_decode_step(const void *weights, void *kv_data, int maxT, int token,
     kv.len = pos;
     gpt2_decode_step_cuda(&GPT2_BACKEND_GEMV, static_cast<const GPT2WeightsGPU *>(weights), &kv,
                           token, pos, &s, static_cast<half *>(logits), static_cast<half *>(caps));
+    return (int)cudaDeviceSynchronize();
+}
+
+// The reference's prefill that fills a sequence's cache (gpt2_prefill_fill_cache, cuda/kvcache.cu:
+// 271-277: gpt2_forward_cuda over d_ids[0..T) with the cache capture, GEMV backend = tiled GEMM + its
+// flash attention) into kv_data (rows 0..T-1 of every layer).
+int ref_gpu_prefill_fill_cache(const void *weights, void *kv_data, int maxT, const int *d_ids, int T) {
+    static GPT2ScratchGPU s;
+    static int have = 0;
+    if (T > maxT || T < 1) return -1;
+    if (have < T) {
+        if (have) gpt2_scratch_free(&s);
+        gpt2_scratch_alloc(&s, T);
+        have = T;
+    }
+    GPT2KVCache kv = view(kv_data, maxT);
+    gpt2_prefill_fill_cache(&GPT2_BACKEND_GEMV, static_cast<const GPT2WeightsGPU *>(weights), &kv, d_ids,
+                            T, &s, nullptr);
+    if (kv.len != T) return -1;
     return (int)cudaDeviceSynchronize();
 }
 

@@ -242,6 +242,72 @@ def test_batch_step_b64_matches_reference(cuda, lib, ref_gpu, weights):
     assert lib.status() == 0
 
 
+@pytest.mark.parametrize("base", [500, 1000])
+def test_batch_step_long_context_b64_matches_reference(cuda, lib, ref_gpu, weights, base):
+    """configs[4] at long context: 64 sequences whose caches were filled by the reference's own
+    prefill forward (gpt2_prefill_fill_cache, cuda/kvcache.cu:271-277) to positions around `base`
+    take one batched step; every sequence's logits and appended K/V are compared with the
+    reference's own decode step (gpt2_decode_step_cuda) from the same cache, and two sequences
+    also go through the single-sequence drop-in gpt2_decode_step_b200."""
+    torch = cuda
+    B, MAXT, NV = 64, 1024, 8  # 8 distinct prompts (lengths base-4 .. base+3), each cache used 8 times
+    rng = np.random.default_rng(base)
+    plen = [base - 4 + v for v in range(NV)]
+    filled = torch.zeros(NV, G.N_LAYER, 2, G.N_HEAD, MAXT, 64, dtype=torch.float16, device="cuda")
+    for v, n in enumerate(plen):
+        ids = torch.from_numpy(rng.integers(0, V, size=n).astype(np.int32)).cuda()
+        ref_gpu.prefill_fill_cache(ctypes.addressof(weights.struct), filled[v].data_ptr(), MAXT,
+                                   ids.data_ptr(), n)
+    arena, kvs = _caches(torch, B, MAXT)
+    for b in range(B):
+        arena[b].copy_(filled[b % NV])
+    pos = [plen[b % NV] for b in range(B)]
+    toks = rng.integers(0, V, size=B).astype(np.int32)
+    bt = Batch(lib, weights, kvs, B)
+    d_tok = torch.from_numpy(toks).cuda()
+    d_pos = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    d_next = torch.empty(B, dtype=torch.int32, device="cuda")
+    logits = torch.empty(B, V, dtype=torch.float16, device="cuda")
+    assert lib.gpt2_b200_batch_step(bt.h, d_tok.data_ptr(), d_pos.data_ptr(), logits.data_ptr(), V,
+                                    d_next.data_ptr(), None) == G.OK
+    torch.cuda.synchronize()
+    assert torch.equal(d_next.long(), logits.float().argmax(dim=1))
+    ref_arena = torch.empty_like(filled[0])
+    ref_logits = torch.empty(V, dtype=torch.float16, device="cuda")
+    worst, worst_kv = 0.0, 0.0
+    for b in range(B):
+        ref_arena.copy_(filled[b % NV])
+        ref_gpu.decode_step(ctypes.addressof(weights.struct), ref_arena.data_ptr(), MAXT, int(toks[b]),
+                            pos[b], ref_logits.data_ptr())
+        torch.cuda.synchronize()
+        err = float((logits[b].float() - ref_logits.float()).abs().max())
+        worst = max(worst, err)
+        assert err <= LOGIT_TOL, f"seq {b} at position {pos[b]}: logits differ by {err:.3e}"
+        p = pos[b]
+        kerr = float((arena[b, :, :, :, p].float() - ref_arena[:, :, :, p].float()).abs().max())
+        worst_kv = max(worst_kv, kerr)
+        assert kerr <= CACHE_TOL, f"seq {b}: K/V appended at {p} differ by {kerr:.3e}"
+        # the step touched only position p
+        assert torch.equal(arena[b, :, :, :, :p], filled[b % NV, :, :, :, :p])
+        assert float(arena[b, :, :, :, p + 1:].abs().max()) == 0.0
+    # the single-sequence drop-in from the same caches
+    one = torch.empty(V, dtype=torch.float16, device="cuda")
+    for b in (0, NV - 1):
+        work = filled[b % NV].clone()
+        kv = G.cache_view(work.data_ptr(), G.N_LAYER, MAXT, length=pos[b])
+        lib.gpt2_decode_step_b200(None, ctypes.byref(weights.struct), ctypes.byref(kv), int(toks[b]),
+                                  pos[b], None, one.data_ptr(), None)
+        assert lib.gpt2_b200_last_error() == G.OK and kv.len == pos[b] + 1
+        ref_arena.copy_(filled[b % NV])
+        ref_gpu.decode_step(ctypes.addressof(weights.struct), ref_arena.data_ptr(), MAXT, int(toks[b]),
+                            pos[b], ref_logits.data_ptr())
+        torch.cuda.synchronize()
+        err = float((one.float() - ref_logits.float()).abs().max())
+        assert err <= LOGIT_TOL, f"drop-in step at {pos[b]}: logits differ by {err:.3e}"
+    assert lib.status() == 0
+    print(f"long context ~{base}: worst logit diff {worst:.3e}, appended K/V diff {worst_kv:.3e}")
+
+
 @pytest.mark.parametrize("B", [100, 256])
 def test_batch_step_large_batches_match_reference(cuda, lib, ref_gpu, weights, B):
     """Padded batches that do not split evenly over the cluster ranks (B = 100 -> 112 columns) and
