@@ -71,9 +71,22 @@ constexpr int OFF_BAR = OFF_OUT + 2 * 4 * OUT_SLOT;
 constexpr int SMEM_BYTES = OFF_BAR + 512;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 constexpr int NSOFT_WARPS = 4;  // per query tile: one warp per TMEM lane quarter
-constexpr int NTHREADS = 32 * (3 + 2 * NSOFT_WARPS);  // producer, 2 MMA issuers, 2 softmax groups
-constexpr int MMA_B_WARP = 2 + 2 * NSOFT_WARPS;              // warp 10 issues query tile B's MMAs
+// Three warpgroups: WG0 = warps 0-3 (warp 0 TMA producer, warps 1 and 2 the MMA issuers of query
+// tiles A and B, warp 3 idle), WG1 = warps 4-7 softmax of A, WG2 = warps 8-11 softmax of B. Each SM
+// sub-partition holds one warp of each group. The launch gives every thread LAUNCH_REGS registers;
+// WG0 then gives registers back (setmaxnreg.dec to WG0_REGS) and the softmax groups take them
+// (setmaxnreg.inc to SOFTMAX_REGS), so the 128 scores of a row stay in registers without spills.
+// The split must add up to the launch's pool exactly: 128 * WG0_REGS + 256 * SOFTMAX_REGS =
+// 384 * LAUNCH_REGS, and the host refuses to launch if ptxas gave the kernel another count.
+constexpr int NTHREADS = 32 * 4 * 3;
+constexpr int MMA_B_WARP = 2;       // warp 2 issues query tile B's MMAs (warp 1: A's)
+constexpr int SOFT_WARP0 = 4;       // first softmax warp
 constexpr int CTAS_PER_SM = 1;
+constexpr int LAUNCH_REGS = 168;    // 65536 / (3 warps per sub-partition x 32), multiple of 8
+constexpr int WG0_REGS = 56;
+constexpr int SOFTMAX_REGS = 224;
+static_assert(128 * WG0_REGS + 256 * SOFTMAX_REGS == NTHREADS * LAUNCH_REGS, "register split");
+static_assert(WG0_REGS + 2 * SOFTMAX_REGS <= 512, "one warp of each group per sub-partition");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TCOL_S = 0;    // + 128 * stream
 constexpr uint32_t TCOL_O = 256;  // + 64 * stream
@@ -776,14 +789,17 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     tc_fence_after();
     const uint32_t tbase = bars->tmem_base;
 
-    if (warp == 0) {
-        if (lane == 0) run_producer<kSplit>(&tm_qkv, &tm_kv, smem, bars, p);
+    if (warp < SOFT_WARP0) {  // WG0: the whole warpgroup gives registers back, then takes its roles
+        reg_dealloc<WG0_REGS>();
+        if (warp == 0) {
+            if (lane == 0) run_producer<kSplit>(&tm_qkv, &tm_kv, smem, bars, p);
+        } else if (warp == 1 || warp == MMA_B_WARP) {
+            if (lane == 0) run_mma<kSplit>(smem, bars, p, tbase, warp == 1 ? 0 : 1);
+        }
         __syncwarp();
-    } else if (warp == 1 || warp == MMA_B_WARP) {
-        if (lane == 0) run_mma<kSplit>(smem, bars, p, tbase, warp == 1 ? 0 : 1);
-        __syncwarp();
-    } else {
-        run_softmax<kSplit>(smem, bars, p, &tm_att, tbase, (warp - 2) / NSOFT_WARPS, warp, lane);
+    } else {  // WG1 / WG2: softmax of query tile A / B
+        reg_alloc<SOFTMAX_REGS>();
+        run_softmax<kSplit>(smem, bars, p, &tm_att, tbase, (warp - SOFT_WARP0) / NSOFT_WARPS, warp, lane);
     }
 
     tc_fence_before();
@@ -899,6 +915,11 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     if (!enc) return GPT2_B200_EDEVICE;
     if (!ctx->prefill_attr_done) {
         for (auto fn : {k_flash_prefill_tc<false>, k_flash_prefill_tc<true>}) {
+            // The warpgroups' register split is sized for exactly LAUNCH_REGS registers per thread at
+            // launch; with any other count the softmax groups' setmaxnreg.inc could not be satisfied.
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) return GPT2_B200_ECUDA;
+            if (fa.numRegs != LAUNCH_REGS) return GPT2_B200_EDEVICE;
             if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
                 cudaSuccess)
                 return GPT2_B200_ECUDA;

@@ -376,6 +376,19 @@ __device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
     return v;
 }
 
+// ---------------------------------------------------------------- per-warpgroup register budget
+// Executed by all 128 threads of a warpgroup: lowers / raises the registers each of its threads may
+// use. Raises wait until other warpgroups of the CTA have released enough, so a split must add up to
+// what the CTA was launched with.
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // Waits until the grids this one depends on (launched with programmatic stream serialization) have
 // completed and their memory is visible; a no-op for an ordinary launch.
