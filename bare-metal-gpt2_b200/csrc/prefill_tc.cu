@@ -8,39 +8,47 @@
 // Here a work item is a PAIR of 128-query tiles (A = tile 2p, B = tile 2p+1) of one head of one
 // sequence, processed against 128-key tiles 0..2p+1 (A stops at its diagonal tile 2p). Each K/V tile
 // is loaded once into shared memory and used by both query tiles, which halves the K/V traffic per
-// FLOP (with one query tile per CTA the K/V re-reads alone kept L2 busy enough to stretch a tile load to
-// ~2 us). The kernel is persistent: one CTA per SM loops over its items (heavy and light pairs in a
-// snake order), with TMEM and barriers set up once and the loads / MMAs of the next item running
-// while the current one finishes. Roles:
+// FLOP. The kernel is persistent: one CTA per SM loops over its items (heavy and light pairs in a
+// snake order), with TMEM and barriers set up once.
+//
+// The work of a CTA is a sequence of UNITS, one query tile against one K/V tile, in the order
+// item by item, K/V tile by K/V tile, A before B. For head_dim 64 a unit's 16,384 exponentials cost
+// each SM sub-partition 1,024 cycles of its MUFU (ex2) pipe against ~680 tensor cycles for the unit's
+// two MMAs (QK at full rate, PV with N = 64 at ~60 %), so the kernel is built to keep the MUFU pipes
+// busy: softmax warps never wait for anything but their next S, and two softmax warps share each
+// sub-partition, their exponential phases overlapping (one warp alone issues ex2 at ~75 % of the
+// pipe's rate, two reach ~90 %). Roles (16 warps, 4 warpgroups):
 //
 //   warp 0   (1 thread)  TMA producer: the two Q tiles of each item (double-buffered), then K(t) and
 //                        V(t-1) tiles (128 x 64 fp16, 128-byte swizzle) straight out of the packed qkv
 //                        rows into 4-stage K and V rings, running ahead across item boundaries.
-//   warps 1, 10 (1 thr)  MMA issuers, one per query tile x: per K/V tile, S_x = Q_x K^T (M128 N128 K64,
-//                        4 x tcgen05.mma K16, operands in shared memory), then O_x += P_x V (M128 N64
-//                        K128, 8 x tcgen05.mma K16, P read from TMEM). Two independent issue streams
-//                        and four accumulators keep the tensor pipe busy; shared-memory descriptors are
-//                        built once and advanced by 32-bit adds.
-//   warps 2-5, 6-9       softmax of query tile A, of query tile B: one thread per query row (TMEM lane),
-//                        all 128 scores of a tile in registers. Log2 domain (1/8 * log2(e) folded into
-//                        one FFMA, hardware ex2); causal mask on the diagonal tile only; P = 2^(s-m)
-//                        written as packed fp16 straight into TMEM; the row sum adds the fp16-rounded
-//                        P values (numerator and denominator use identical weights); O is rescaled in
-//                        TMEM only when the running max grows by more than 2^8 (the stale max is
-//                        otherwise kept for both l and O: exact, and P <= 256). The A and B warps that
-//                        share an SM sub-partition take turns on its MUFU (ex2) pipe (A may run one
-//                        turn ahead). Epilogue: O / l -> fp16 -> a swizzled 4 KB shared-memory slot per
-//                        warp -> one TMA store of the warp's 32 rows, so output rows leave as whole
-//                        128-byte lines.
+//   warps 2, 1           MMA issuers for both query tiles, in unit order. Warp 2: S_u = Q K^T into one of
+//                        three TMEM S buffers (M128 N128 K64, 4 x tcgen05.mma K16), issued as soon as
+//                        the PV of unit u-3 (the buffer's previous user) has completed. Warp 1: O_x +=
+//                        P_u V (M128 N64 K128, 8 x tcgen05.mma K16, P read from TMEM) once the softmax
+//                        has written P_u.
+//   warps 4-7, 8-11      softmax of query tile A, of B: one thread per query row (TMEM lane), all 128
+//                        scores of a unit in registers. Log2 domain (1/8 * log2(e) folded into one
+//                        FFMA, hardware ex2); causal mask on the diagonal tile only; P = 2^(s-m) written
+//                        as packed fp16 over the first 64 columns of the unit's own S buffer; the row
+//                        sum adds the fp16-rounded P values (numerator and denominator use identical
+//                        weights); O is rescaled in TMEM only when the running max grows by more than
+//                        2^8 (the stale max is otherwise kept for both l and O: exact, and P <= 256).
+//   warps 12-15          epilogue of both query tiles: at the end of an item, O / l -> fp16 -> a
+//                        swizzled 4 KB shared-memory slot per warp -> one TMA store of the warp's 32
+//                        rows, so output rows leave as whole 128-byte lines; the split path's partial
+//                        rows and merge (below) also run here.
 //
 // Launches with fewer whole pairs than SMs (one layer of one sequence) run the kSplit instantiation: a
 // work unit is a chunk of a pair's key range; split units park unnormalised rows (o, m, l) in a
 // workspace and the last chunk to arrive for a 32-row group merges them. With a KV-cache target the
 // producer also stores the K/V tiles its unit owns into the cache, straight from the ring.
 //
-// TMEM: all 512 columns (S_A 0, S_B 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory: 224.5 KB
-// (Q 64 KB, K and V rings 128 KB, output slots 32 KB, barriers). No cluster, no multicast. Every
-// mbarrier wait is bounded.
+// TMEM: all 512 columns (S buffers at 0, 128, 256; O_A 384, O_B 448). Shared memory: Q 64 KB, K and V
+// rings 128 KB, output slots 16 KB, row statistics 4 KB, barriers. No cluster, no multicast. Every
+// mbarrier wait is bounded. Registers: the launch gives each of the 512 threads 128; the producer /
+// MMA warpgroup and the epilogue warpgroup hand some back (setmaxnreg) so that the softmax warps hold
+// their 128 scores without spilling.
 //
 // Launch: a programmatic dependent of the previous kernel in the stream. Barrier init, TMEM
 // allocation and an L2 prefetch of the first item's Q, K and V tiles overlap that kernel's tail;
@@ -64,56 +72,59 @@ constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB: 128 rows x 128 B
 constexpr int OFF_Q = 0;                                     // [NQ][2 tiles]
 constexpr int OFF_K = OFF_Q + NQ * 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + NSTAGE * TILE_BYTES;
-constexpr int OUT_ROWS = 32;                    // output rows per softmax warp (one TMA store box)
+constexpr int OUT_ROWS = 32;                    // output rows per epilogue warp (one TMA store box)
 constexpr int OUT_SLOT = OUT_ROWS * HD * 2;     // 4 KB: 32 rows x 128 B, 128-byte swizzle
-constexpr int OFF_OUT = OFF_V + NSTAGE * TILE_BYTES;  // [2 query tiles][4 warps] output slots
-constexpr int OFF_BAR = OFF_OUT + 2 * 4 * OUT_SLOT;
+constexpr int OFF_OUT = OFF_V + NSTAGE * TILE_BYTES;  // [4 epilogue warps] output slots
+constexpr int OFF_STATS = OFF_OUT + 4 * OUT_SLOT;     // [2 tiles][2 item parities][m | l][128 rows] fp32
+constexpr int OFF_BAR = OFF_STATS + 2 * 2 * 2 * BM * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 constexpr int NSOFT_WARPS = 4;  // per query tile: one warp per TMEM lane quarter
-// Three warpgroups: WG0 = warps 0-3 (warp 0 TMA producer, warps 1 and 2 the MMA issuers of query
-// tiles A and B, warp 3 idle), WG1 = warps 4-7 softmax of A, WG2 = warps 8-11 softmax of B. Each SM
-// sub-partition holds one warp of each group. The launch gives every thread LAUNCH_REGS registers;
-// WG0 then gives registers back (setmaxnreg.dec to WG0_REGS) and the softmax groups take them
-// (setmaxnreg.inc to SOFTMAX_REGS), so the 128 scores of a row stay in registers without spills.
-// The split must add up to the launch's pool exactly: 128 * WG0_REGS + 256 * SOFTMAX_REGS =
-// 384 * LAUNCH_REGS, and the host refuses to launch if ptxas gave the kernel another count.
-constexpr int NTHREADS = 32 * 4 * 3;
-constexpr int MMA_B_WARP = 2;       // warp 2 issues query tile B's MMAs (warp 1: A's)
-constexpr int SOFT_WARP0 = 4;       // first softmax warp
+// Four warpgroups, one warp of each on every SM sub-partition: WG0 = warps 0-3 (producer, the two MMA
+// issuers, one idle warp), WG1 = softmax of A, WG2 = softmax of B, WG3 = epilogue. The launch gives every
+// thread LAUNCH_REGS registers; WG0 and WG3 give some back (setmaxnreg.dec) and the softmax groups
+// take them (setmaxnreg.inc). The split adds up to the launch's pool exactly, and the host refuses to
+// launch if ptxas gave the kernel another register count (an .inc could then never be satisfied).
+constexpr int NTHREADS = 32 * 4 * 4;
+constexpr int MMA_WARP = 1;      // query tile A's MMA issuer (and TMEM allocation)
+constexpr int MMA_B_WARP = 2;    // query tile B's MMA issuer
+constexpr int SOFT_WARP0 = 4;   // first softmax warp
+constexpr int EPI_WARP0 = 12;   // first epilogue warp
 constexpr int CTAS_PER_SM = 1;
-constexpr int LAUNCH_REGS = 168;    // 65536 / (3 warps per sub-partition x 32), multiple of 8
-constexpr int WG0_REGS = 56;
-constexpr int SOFTMAX_REGS = 224;
-static_assert(128 * WG0_REGS + 256 * SOFTMAX_REGS == NTHREADS * LAUNCH_REGS, "register split");
-static_assert(WG0_REGS + 2 * SOFTMAX_REGS <= 512, "one warp of each group per sub-partition");
+constexpr int LAUNCH_REGS = 128;  // 65536 / (4 warps per sub-partition x 32)
+constexpr int WG0_REGS = 64;
+constexpr int EPI_REGS = 80;
+constexpr int SOFTMAX_REGS = 184;
+static_assert(128 * (WG0_REGS + EPI_REGS) + 256 * SOFTMAX_REGS == NTHREADS * LAUNCH_REGS, "register split");
+static_assert(WG0_REGS + EPI_REGS + 2 * SOFTMAX_REGS <= 512, "one warp of each group per sub-partition");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TCOL_S = 0;    // + 128 * stream
-constexpr uint32_t TCOL_O = 256;  // + 64 * stream
-constexpr uint32_t TCOL_P = 384;  // + 64 * stream
+constexpr uint32_t TCOL_S = 0;    // + 128 * query tile
+constexpr uint32_t TCOL_O = 256;  // + 64 * query tile
+constexpr uint32_t TCOL_P = 384;  // + 64 * query tile
 constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);  // Q K-major, K K-major
 constexpr uint32_t IDESC_O = idesc_f16_f32(BM, HD, 0, 1);  // P K-major (TMEM), V MN-major
 constexpr float RESCALE_THRESHOLD = 8.0f;                  // log2 units: P stays <= 2^8
-constexpr int A_TURN_SLACK = 1;  // ex2 phases query tile A may run ahead of B on a sub-partition
 
 struct Stream {  // per query tile of the pair
-    uint64_t s_full;   // its QK of the current K/V tile is done
-    uint64_t s_free;   // its softmax warps have read S
+    uint64_t s_full;   // its QK of the current K/V tile has completed
+    uint64_t s_free;   // its softmax warps have read S into registers
     uint64_t p_full;   // its softmax warps have written P (and rescaled O)
-    uint64_t o_done;   // its PV of the current tile is done
-    uint64_t o_free;   // its epilogue has read O of the current item
-    uint64_t drain;    // teardown: every MMA of this query tile's issuing thread has completed
-    int ex2_done[4];   // per lane quarter (= SM sub-partition): ex2 phases completed by its warp
+    uint64_t o_done;   // a PV of this query tile has completed (one phase per PV)
+    uint64_t o_last;   // the item's last PV of this query tile has completed (one phase per item)
+    uint64_t o_free;   // the epilogue has read O of the item
 };
 
 struct __align__(8) Bars {
     uint64_t q_full[NQ];
-    uint64_t q_empty[NQ];
+    uint64_t q_empty[NQ];      // the item's last QK has completed
     uint64_t k_full[NSTAGE];
-    uint64_t k_empty[NSTAGE];  // the QKs that read this K stage have completed
+    uint64_t k_empty[NSTAGE];  // the last QK reading this K stage has completed
     uint64_t v_full[NSTAGE];
-    uint64_t v_empty[NSTAGE];  // the PVs that read this V stage have completed
-    Stream st[2];
+    uint64_t v_empty[NSTAGE];  // the last PV reading this V stage has completed
+    Stream st[2];              // per query tile
+    uint64_t st_full[2][2];    // softmax of tile x wrote its item's row statistics (buffer = item parity)
+    uint64_t st_free[2][2];    // the epilogue has read them
+    uint64_t drain;            // teardown: every MMA of both issuers has completed
     uint32_t tmem_base;
     int abort;
 };
@@ -135,6 +146,8 @@ struct Params {
     unsigned *counters;        // split units: arrivals per [group][lane quarter], re-armed to 0
     unsigned *status;
     unsigned long long timeout_ns;
+    __half *att;               // split launches: output rows are stored directly (no TMA slot)
+    long long att_seq_stride;  // elements between sequences of att
 };
 constexpr int PART_COLS = HD + 2;  // o[64], m, l of a row; stored column-major (coalesced)
 constexpr int MAX_CHUNKS = 8;       // chunks per pair at most (the merge is unrolled over them)
@@ -325,27 +338,45 @@ __device__ void run_producer(const CUtensorMap *tm, const CUtensorMap *tm_kv, ui
     }
 }
 
-// ------------------------------------------------------------------ MMA issuers (one thread per query tile)
-// Each query tile x has its own issuing thread, so neither stream's MMAs queue behind the other's
-// dependencies. Both walk every K/V tile of every item; the shared K, V and Q stages are released
-// through two-arrival barriers: a stream commits its MMAs on them (or, for a tile it does not use,
-// arrives after that tile has landed, so that arrivals of different phases cannot mix).
+// ------------------------------------------------------------------ MMA issuers (one warp per query tile)
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
+                                          unsigned long long to) {
+    const bool ok = mbar_wait(bar, parity, to);
+    return __all_sync(0xffffffffu, ok);
+}
+
+struct Descs {
+    uint32_t q_lo, q_hi, k_lo, k_hi, v_lo, v_hi;
+    __device__ __forceinline__ explicit Descs(uint8_t *smem) {
+        // Built once; an MMA then only adds a K-step offset to the start-address word (+32 B per K16
+        // step inside a 128-byte swizzled row, +2 KB = 16 rows of V per K16 step).
+        const uint64_t dq0 = sdesc_sw128(smem_u32(smem + OFF_Q), 16, 1024);
+        const uint64_t dk0 = sdesc_sw128(smem_u32(smem + OFF_K), 16, 1024);
+        const uint64_t dv0 = sdesc_sw128(smem_u32(smem + OFF_V), TILE_BYTES, 1024);
+        q_lo = static_cast<uint32_t>(dq0);
+        q_hi = static_cast<uint32_t>(dq0 >> 32);
+        k_lo = static_cast<uint32_t>(dk0);
+        k_hi = static_cast<uint32_t>(dk0 >> 32);
+        v_lo = static_cast<uint32_t>(dv0);
+        v_hi = static_cast<uint32_t>(dv0 >> 32);
+    }
+};
+constexpr uint32_t TILE_DESC = TILE_BYTES >> 4;  // one 16 KB tile in start-address units
+
+// Warp 1 issues query tile A's MMAs, warp 2 tile B's, each walking every K/V tile of every item: S_x =
+// Q_x K^T once the softmax has read the previous S_x, O_x += P_x V once it has written P_x. Each issuer
+// runs on its whole warp (every wait and all bookkeeping warp-uniform, so the MMA operands stay in
+// uniform registers); one elected lane issues the MMAs and commits. The shared K, V and Q stages are
+// released through two-arrival barriers: a tile's MMAs commit on them (or, for a tile it does not use,
+// the issuer arrives after that tile has landed, so arrivals of different phases cannot mix).
 template <bool kSplit>
 __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int x) {
     const unsigned long long to = p.timeout_ns;
+    const Descs ds(smem);
+    const bool leader = elect_one();
     Stream &S = bars->st[x];
-    // Descriptors are built once; an MMA then only adds a K-step offset to the start-address word
-    // (+32 B per K16 step inside a 128-byte swizzled row, +2 KB = 16 rows of V per K16 step).
-    const uint64_t dq0 = sdesc_sw128(smem_u32(smem + OFF_Q), 16, 1024);
-    const uint64_t dk0 = sdesc_sw128(smem_u32(smem + OFF_K), 16, 1024);
-    const uint64_t dv0 = sdesc_sw128(smem_u32(smem + OFF_V), TILE_BYTES, 1024);
-    const uint32_t q_lo = static_cast<uint32_t>(dq0), q_hi = static_cast<uint32_t>(dq0 >> 32);
-    const uint32_t k_lo = static_cast<uint32_t>(dk0), k_hi = static_cast<uint32_t>(dk0 >> 32);
-    const uint32_t v_lo = static_cast<uint32_t>(dv0), v_hi = static_cast<uint32_t>(dv0 >> 32);
-    constexpr uint32_t TILE_DESC = TILE_BYTES >> 4;  // one 16 KB tile in start-address units
     const uint32_t tS = tbase + TCOL_S + 128 * x, tO = tbase + TCOL_O + 64 * x;
     const uint32_t tP = tbase + TCOL_P + 64 * x;
-
     int gs = 0;   // this query tile's QKs issued (all items)
     int gp = 0;   // this query tile's PVs issued
     int itp = 0;  // items in which this query tile's PVs have started (for o_free)
@@ -353,51 +384,59 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
     auto qk_step = [&](const Cursor<kSplit> &q) -> bool {
         const int qb = q.it % NQ, s = q.g % NSTAGE;
         const bool uses = q.j < q.I.nk_of(x);
-        if (q.j == 0 && !mbar_wait(&bars->q_full[qb], (q.it / NQ) & 1, to)) return false;
-        if (!mbar_wait(&bars->k_full[s], (q.g / NSTAGE) & 1, to)) return false;
+        if (q.j == 0 && !warp_wait(&bars->q_full[qb], (q.it / NQ) & 1, to)) return false;
+        if (!warp_wait(&bars->k_full[s], (q.g / NSTAGE) & 1, to)) return false;
         if (uses) {
-            if (gs > 0 && !mbar_wait(&S.s_free, (gs - 1) & 1, to)) return false;
+            if (gs > 0 && !warp_wait(&S.s_free, (gs - 1) & 1, to)) return false;
             tc_fence_after();
-            const uint32_t a = q_lo + (qb * 2 + x) * TILE_DESC, b = k_lo + s * TILE_DESC;
+            const uint32_t a = ds.q_lo + (qb * 2 + x) * TILE_DESC, b = ds.k_lo + s * TILE_DESC;
+            if (leader) {
 #pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk)
-                umma_f16_ss_lohi(tS, a + 2 * kk, q_hi, b + 2 * kk, k_hi, IDESC_S, kk > 0 ? 1u : 0u);
-            umma_commit(&S.s_full);
-            umma_commit(&bars->k_empty[s]);
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    umma_f16_ss_lohi(tS, a + 2 * kk, ds.q_hi, b + 2 * kk, ds.k_hi, IDESC_S, kk > 0 ? 1u : 0u);
+                umma_commit(&S.s_full);
+                umma_commit(&bars->k_empty[s]);
+            }
             ++gs;
-        } else {
+        } else if (leader) {
             mbar_arrive(&bars->k_empty[s]);
         }
-        // the Q buffer: released after this stream's last QK of the item (or at once if it has none)
+        // the Q buffer: released after this query tile's last QK of the item (or at once if it has none)
         const int last = q.I.nk_of(x) ? q.I.nk_of(x) - 1 : 0;
-        if (q.j == last) {
+        if (q.j == last && leader) {
             if (uses) umma_commit(&bars->q_empty[qb]);
             else mbar_arrive(&bars->q_empty[qb]);
         }
+        __syncwarp();
         return true;
     };
     // O += P V for the K/V tile under cursor v (or release of that tile).
     auto pv_step = [&](const Cursor<kSplit> &v) -> bool {
         const int s = v.g % NSTAGE;
-        if (!mbar_wait(&bars->v_full[s], (v.g / NSTAGE) & 1, to)) return false;
+        if (!warp_wait(&bars->v_full[s], (v.g / NSTAGE) & 1, to)) return false;
         if (v.j >= v.I.nk_of(x)) {
-            mbar_arrive(&bars->v_empty[s]);
+            if (leader) mbar_arrive(&bars->v_empty[s]);
+            __syncwarp();
             return true;
         }
-        if (!mbar_wait(&S.p_full, gp & 1, to)) return false;
-        if (v.j == 0) {
-            if (itp > 0 && !mbar_wait(&S.o_free, (itp - 1) & 1, to)) return false;
+        if (!warp_wait(&S.p_full, gp & 1, to)) return false;
+        if (v.j == 0) {  // the item's first PV overwrites O: the epilogue must have read it
+            if (itp > 0 && !warp_wait(&S.o_free, (itp - 1) & 1, to)) return false;
             ++itp;
         }
         tc_fence_after();
-        const uint32_t b = v_lo + s * TILE_DESC;
-        umma_f16_ts_lohi(tO, tP, b, v_hi, IDESC_O, v.j == 0 ? 0u : 1u);
+        const uint32_t b = ds.v_lo + s * TILE_DESC;
+        if (leader) {
+            umma_f16_ts_lohi(tO, tP, b, ds.v_hi, IDESC_O, v.j == 0 ? 0u : 1u);
 #pragma unroll
-        for (int kk = 1; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P per step
-            umma_f16_ts_lohi(tO, tP + kk * 8, b + 128 * kk, v_hi, IDESC_O, 1u);
-        umma_commit(&S.o_done);
-        umma_commit(&bars->v_empty[s]);
+            for (int kk = 1; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P per step
+                umma_f16_ts_lohi(tO, tP + kk * 8, b + 128 * kk, ds.v_hi, IDESC_O, 1u);
+            umma_commit(&S.o_done);
+            if (v.j == v.I.nk_of(x) - 1) umma_commit(&S.o_last);
+            umma_commit(&bars->v_empty[s]);
+        }
         ++gp;
+        __syncwarp();
         return true;
     };
 
@@ -410,6 +449,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
         q.advance(p);
     }
     while (ok && v.valid) {
+        if (aborted(bars)) break;
         if (q.valid) {
             ok = qk_step(q);
             if (!ok) break;
@@ -419,54 +459,165 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
         if (!ok) break;
         v.advance(p);
     }
-    if (!ok) raise_abort(bars, p.status, ST_PREFILL_MMA_TIMEOUT);
-    // Teardown guard: all MMAs issued by this thread complete before TMEM is released.
-    umma_commit(&S.drain);
-    if (!mbar_wait(&S.drain, 0, to)) atomicOr(p.status, ST_PREFILL_DRAIN_TIMEOUT);
+    if (!ok && leader) raise_abort(bars, p.status, ST_PREFILL_MMA_TIMEOUT);
+    // Teardown guard: all MMAs issued by this warp complete before TMEM is released.
+    if (leader) umma_commit(&bars->drain);
+    __syncwarp();
 }
 
-// ------------------------------------------------------------------ softmax + epilogue
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
-                                          unsigned long long to) {
-    const bool ok = mbar_wait(bar, parity, to);
-    return __all_sync(0xffffffffu, ok);
+// ------------------------------------------------------------------ softmax
+
+// End of an item in a split launch, run by the item's softmax warps (32 rows each): once the item's
+// last PV of this query tile has completed, O / l goes straight to att when the item is a whole pair;
+// a chunk of a pair parks its unnormalised rows (o, m, l) in the workspace and the last chunk to
+// arrive for these 32 rows merges every chunk's partial. Rows are stored as whole 128-byte lines.
+// Returns false when a wait expired.
+__device__ __forceinline__ bool split_epilogue(Bars *bars, const Params &p, uint32_t tO, int x, int quarter,
+                                            int lane, int row, int it, int g, float m_row, float l_row) {
+    Stream &S = bars->st[x];
+    if (!warp_wait(&S.o_done, (g - 1) & 1, p.timeout_ns)) return false;  // the item's last PV
+    tc_fence_after();
+    Item I;
+    get_item<true>(p, it, I);
+    const int qrow = (2 * I.pair + x) * BM + row;  // query index of this thread's row
+    uint4 *dst = reinterpret_cast<uint4 *>(p.att + I.b * p.att_seq_stride +
+                                           static_cast<long long>(qrow) * p.E + I.h * HD);
+    auto store_row = [&](const float (&o)[32], int half) {  // 32 columns of this row, normalised
+        if (qrow < p.T) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                dst[4 * half + q] = make_uint4(pack_half2(o[8 * q], o[8 * q + 1]), pack_half2(o[8 * q + 2], o[8 * q + 3]),
+                                               pack_half2(o[8 * q + 4], o[8 * q + 5]), pack_half2(o[8 * q + 6], o[8 * q + 7]));
+        }
+    };
+    if (I.nchunk == 1) {
+        const float inv_l = 1.f / l_row;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+            uint32_t v[32];
+            tmem_ld32(tO + 32 * cb, v);
+            tmem_wait_ld();
+            float o[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]) * inv_l;
+            store_row(o, cb);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.o_free);
+        return true;
+    }
+    const long long grp = ((static_cast<long long>(I.b) * p.H + I.h) * p.n_pairs + I.pair) * 2 + x;
+    // column c of this row of chunk k at part[((grp * max_chunks + k) * PART_COLS + c) * 128 + row]
+    float *mine = p.part + (grp * p.max_chunks + I.chunk) * (PART_COLS * BM) + row;
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+        uint32_t v[32];
+        tmem_ld32(tO + 32 * cb, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) __stcg(mine + (32 * cb + i) * BM, __uint_as_float(v[i]));
+    }
+    __stcg(mine + HD * BM, m_row);
+    __stcg(mine + (HD + 1) * BM, l_row);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
+    // Publish the warp's 32 partial rows and count this chunk's arrival in one release-acquire atomic
+    // (the warp barrier orders every lane's stores before lane 0's release; the last arrival's acquire
+    // makes every chunk's rows visible to the merge below).
+    unsigned *cnt = p.counters + grp * 4 + quarter;
+    const int ncx = (2 * I.pair + x + p.kv_chunk) / p.kv_chunk;  // chunks with this tile's keys
+    unsigned prev = 0;
+    if (lane == 0)
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != static_cast<unsigned>(ncx - 1)) return true;
+    // last chunk of these 32 rows: merge every chunk's partial row
+    const float *base = p.part + grp * p.max_chunks * (PART_COLS * BM) + row;
+    constexpr int CH = PART_COLS * BM;  // floats per chunk
+    // Loads are predicated rather than branched so that each batch is one L2 round trip: (m, l) of
+    // every chunk, then per 32-column half up to 4 chunks' values at once.
+    float mk[MAX_CHUNKS], lk[MAX_CHUNKS], w[MAX_CHUNKS];
+#pragma unroll
+    for (int k = 0; k < MAX_CHUNKS; ++k) {
+        mk[k] = -INFINITY;
+        lk[k] = 0.f;
+        if (k < ncx) {
+            mk[k] = __ldcg(base + k * CH + HD * BM);
+            lk[k] = __ldcg(base + k * CH + (HD + 1) * BM);
+        }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < MAX_CHUNKS; ++k) M = fmaxf(M, k < ncx ? mk[k] : -INFINITY);
+    float L = 0.f;
+#pragma unroll
+    for (int k = 0; k < MAX_CHUNKS; ++k) {
+        w[k] = k < ncx ? ex2_approx(mk[k] - M) : 0.f;
+        L = fmaf(w[k], lk[k], L);
+    }
+    const float inv_l = 1.f / L;
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int k0 = 0; k0 < MAX_CHUNKS; k0 += 4) {
+            if (k0 < ncx) {
+                float vals[4][32];
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float *pc = base + (k0 + kk) * CH + (32 * cb) * BM;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) vals[kk][i] = 0.f;
+                    if (k0 + kk < ncx) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) vals[kk][i] = __ldcg(pc + i * BM);
+                    }
+                }
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = fmaf(w[k0 + kk], vals[kk][i], acc[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] *= inv_l;
+        store_row(acc, cb);
+    }
+    if (lane == 0) *cnt = 0u;  // re-armed for the next launch (every chunk has arrived)
+    return true;
 }
 
 // Softmax of query tile x (0 = A, 1 = B) of every item: 4 warps, thread = one query row (TMEM lane),
-// all 128 scores of a tile in registers.
+// all 128 scores of a tile in registers. S is released as soon as it is in registers (the next QK
+// runs while this tile is processed). The packed P values are kept in registers until every
+// exponential is done; only then does the warp wait for the previous PV of its query tile (which read
+// the P buffer, and after which O may be rescaled) -- by that time it has long completed. Every
+// o_done phase is waited in order.
 template <bool kSplit>
-__device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CUtensorMap *tm_att,
-                            uint32_t tbase, int x, int warp, int lane) {
+__device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t tbase, int x,
+                            int warp, int lane) {
     const unsigned long long to = p.timeout_ns;
     Stream &S = bars->st[x];
-    Stream &O = bars->st[x ^ 1];  // the other query tile
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access (= SM sub-partition)
+    const int row = quarter * 32 + lane;
     const uint32_t tl = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t tS = tl + TCOL_S + 128 * x;
     const uint32_t tO = tl + TCOL_O + 64 * x;
     const uint32_t tP = tl + TCOL_P + 64 * x;
     const float c = p.scale_log2;
-
-    int g = 0;  // this query tile's K/V tiles processed so far (all items)
-    // Ping-pong on the MUFU: the ex2 loops of the A warp and the B warp that share an SM
-    // sub-partition alternate, in the order A0 B0 A1 B1 ... of each item (B's extra diagonal tile
-    // follows its own previous one). ocum = ex2 phases the other query tile completed in earlier
-    // items; before our phase k of an item we wait until the other tile's warp on this sub-partition
-    // has completed ocum + min(k + x, nk_other) phases (x = 0 for A, 1 for B), less A_TURN_SLACK for
-    // A: A may run one phase ahead, so at an item switch it does not idle through B's diagonal tile
-    // and B's epilogue (measured: -6 % at P=2048, -10 % for one layer at P=1024). The counts are
-    // monotonic shared-memory counters (a parity barrier would alias: at an item boundary B runs two
-    // phases in a row, so A may need a count two ahead of the current one). They only order work;
-    // no data passes through them.
-    int ocum = 0;
-    int ex2_phases = 0;  // this warp's completed ex2 phases
+    float *stats = reinterpret_cast<float *>(smem + OFF_STATS);
+    int g = 0;   // this query tile's K/V tiles processed so far (all items)
+    int kx = 0;  // items in which this query tile has keys (statistics buffer)
     bool ok = true;
     Item I;
-    for (int it = 0; ok && get_item<kSplit>(p, it, I); ocum += I.nk_of(x ^ 1), ++it) {
+    for (int it = 0; ok && get_item<kSplit>(p, it, I); ++it) {
         const int nk = I.nk_of(x);
-        if (nk == 0) continue;     // this query tile has no keys in this unit
-        const int nk_other = I.nk_of(x ^ 1);
-        const int diag_j = 2 * I.pair + x - I.kv0;  // unit tile holding this tile's diagonal
+        if (nk == 0) continue;     // this query tile has no keys in this unit of work
+        const int diag_j = 2 * I.pair + x - I.kv0;  // K/V tile holding this tile's diagonal
         float m_used = -INFINITY;  // running max (log2 units) used for the exponentials
         float l = 0.f;             // running sum of the (fp16-rounded) exponentials
         for (int j = 0; j < nk; ++j, ++g) {
@@ -487,12 +638,10 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.s_free);  // the next QK may overwrite S
-
             if (j == diag_j) {  // diagonal tile (BM == BN): key k is visible iff k <= r
-                const int r = quarter * 32 + lane;
 #pragma unroll
                 for (int i = 0; i < BN; ++i)
-                    if (i > r) xs[i] = -INFINITY;
+                    if (i > row) xs[i] = -INFINITY;
             }
             float pm[8];  // independent partial maxima, three-input max
 #pragma unroll
@@ -512,61 +661,29 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
                 resc = true;
             }
             const float neg_m = -m_used;
-            if (g > 0) {  // the previous PV of this query tile is done: P may be overwritten and O
-                          // holds its result
-                ok = warp_wait(&S.o_done, (g - 1) & 1, to);
-                if (!ok) break;
-                tc_fence_after();
-            }
-            {  // wait for our turn on this sub-partition's MUFU (time-bounded spin on the counter)
-                const int need = ocum + min(j + x, nk_other) - (x == 0 ? A_TURN_SLACK : 0);
-                int ready = 1;
-                if (lane == 0 && need > 0) {
-                    const volatile int *cnt = &O.ex2_done[quarter];
-                    uint64_t t0 = 0;
-                    for (int spin = 0;; ++spin) {
-                        if (*cnt >= need) break;
-                        if (spin == 32) t0 = globaltimer_ns();
-                        if (spin > 32) {
-                            if (globaltimer_ns() - t0 > to) {
-                                ready = 0;
-                                break;
-                            }
-                            __nanosleep(32);
-                        }
-                    }
-                }
-                ok = __shfl_sync(0xffffffffu, ready, 0) != 0;
-                if (!ok) break;
-            }
-            // P = 2^(s - m) as packed fp16, 32 keys at a time straight into TMEM. The row sum adds the
-            // fp16-ROUNDED values (the ones the PV MMA consumes).
+            // P = 2^(s - m) as packed fp16 (kept in registers). The row sum adds the fp16-ROUNDED values
+            // (the ones the PV MMA consumes).
+            uint32_t pk[4][16];
             float ps[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) ps[k] = 0.f;
-            auto exp_chunk = [&](const int cb, uint32_t(&pk)[16]) {
+#pragma unroll
+            for (int cb = 0; cb < 4; ++cb) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const float p0 = ex2_approx(fmaf(xs[32 * cb + 2 * i], c, neg_m));
                     const float p1 = ex2_approx(fmaf(xs[32 * cb + 2 * i + 1], c, neg_m));
-                    pk[i] = pack_half2(p0, p1);
-                    ps[(2 * i) & 7] = add_f16lo_f32(pk[i], ps[(2 * i) & 7]);
-                    ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[i], ps[(2 * i + 1) & 7]);
+                    pk[cb][i] = pack_half2(p0, p1);
+                    ps[(2 * i) & 7] = add_f16lo_f32(pk[cb][i], ps[(2 * i) & 7]);
+                    ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[cb][i], ps[(2 * i + 1) & 7]);
                 }
-            };
-#pragma unroll
-            for (int cb = 0; cb < 4; ++cb) {
-                uint32_t pk[16];
-                exp_chunk(cb, pk);
-                if (cb == 3) {  // last exponentials computed: the other warp may take the MUFU
-                    ++ex2_phases;
-                    if (lane == 0)  // (the value depends on the last ex2, so it is not stored earlier)
-                        *reinterpret_cast<volatile int *>(&S.ex2_done[quarter]) =
-                            ex2_phases + (pk[15] == 0xFFFFFFFFu ? 1 : 0);
-                }
-                tmem_st16(tP + 16 * cb, pk);
             }
             l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            if (g > 0) {  // the previous PV of this query tile has read P and written O
+                ok = warp_wait(&S.o_done, (g - 1) & 1, to);
+                if (!ok) break;
+                tc_fence_after();
+            }
             if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll
                 for (int cb = 0; cb < 2; ++cb) {
@@ -578,145 +695,103 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, const CU
                     tmem_st32(tO + 32 * cb, v);
                 }
             }
+#pragma unroll
+            for (int cb = 0; cb < 4; ++cb) tmem_st16(tP + 16 * cb, pk[cb]);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.p_full);
         }
         if (!ok) break;
-        // ---- epilogue of this unit: O / l -> fp16 -> this warp's output slot -> one TMA store of
-        // its 32 rows (rows past T are clipped by the tensor map). A split unit first parks its
-        // unnormalised rows in the workspace; the last chunk to arrive merges them.
-        ok = warp_wait(&S.o_done, (g - 1) & 1, to);
-        if (!ok) break;
-        tc_fence_after();
-        if (kSplit) get_item<kSplit>(p, it, I);  // re-derived, not kept live through the tile loop
-        // the slot's previous store has finished reading it (returns at once if none is pending)
-        if (lane == 0) bulk_wait_group_read0();
-        __syncwarp();
-        // This warp's output slot: its 32 rows x 64 columns, row `lane` at lane * 128 B, 16-byte
-        // chunk k of a row at chunk position k ^ (row % 8) (the TMA 128-byte swizzle, which also
-        // makes these writes bank-conflict-free).
-        uint8_t *my_row = smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT + lane * (HD * 2);
-        auto put32 = [&](int cb, const uint32_t(&o)[16]) {  // 32 fp16 columns of this row
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int chunk = (4 * cb + q) ^ (lane & 7);
-                *reinterpret_cast<uint4 *>(my_row + chunk * 16) =
-                    make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-            }
-        };
-        bool store = true;  // this warp holds the final rows of its 32 queries
-        if (!kSplit || I.nchunk == 1) {
-            const float inv_l = 1.f / l;
-            uint32_t v[2][32];  // both halves of the row in flight before one wait
-            tmem_ld32(tO, v[0]);
-            tmem_ld32(tO + 32, v[1]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int cb = 0; cb < 2; ++cb) {  // 32 columns of O at a time
-                uint32_t o[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    o[i] = pack_half2(__uint_as_float(v[cb][2 * i]) * inv_l,
-                                      __uint_as_float(v[cb][2 * i + 1]) * inv_l);
-                put32(cb, o);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
-        } else {
-            const long long grp =
-                ((static_cast<long long>(I.b) * p.H + I.h) * p.n_pairs + I.pair) * 2 + x;
-            const int row = quarter * OUT_ROWS + lane;
-            // column c of this row of chunk k at part[((grp * max_chunks + k) * PART_COLS + c) * 128 + row]
-            float *mine = p.part + (grp * p.max_chunks + I.chunk) * (PART_COLS * BM) + row;
-#pragma unroll
-            for (int cb = 0; cb < 2; ++cb) {
-                uint32_t v[32];
-                tmem_ld32(tO + 32 * cb, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) mine[(32 * cb + i) * BM] = __uint_as_float(v[i]);
-            }
-            mine[HD * BM] = m_used;
-            mine[(HD + 1) * BM] = l;
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.o_free);
-            __threadfence();  // this row's partial is visible device-wide before the arrival
-            __syncwarp();
-            unsigned *cnt = p.counters + grp * 4 + quarter;
-            const int ncx = (2 * I.pair + x + p.kv_chunk) / p.kv_chunk;  // chunks with this tile's keys
-            unsigned prev = 0;
-            if (lane == 0) prev = atomicAdd(cnt, 1u);
-            prev = __shfl_sync(0xffffffffu, prev, 0);
-            store = (prev == static_cast<unsigned>(ncx - 1));
-            if (store) {  // last chunk of these 32 rows: merge every chunk's partial row
-                __threadfence();
-                const float *base = p.part + grp * p.max_chunks * (PART_COLS * BM) + row;
-                constexpr int CH = PART_COLS * BM;  // floats per chunk
-                // Loads are predicated rather than branched so that each batch is one L2 round trip:
-                // (m, l) of every chunk, then per 32-column half up to 4 chunks' values at once.
-                float mk[MAX_CHUNKS], lk[MAX_CHUNKS], w[MAX_CHUNKS];
-#pragma unroll
-                for (int k = 0; k < MAX_CHUNKS; ++k) {
-                    mk[k] = -INFINITY;
-                    lk[k] = 0.f;
-                    if (k < ncx) {
-                        mk[k] = __ldcg(base + k * CH + HD * BM);
-                        lk[k] = __ldcg(base + k * CH + (HD + 1) * BM);
-                    }
-                }
-                float M = -INFINITY;
-#pragma unroll
-                for (int k = 0; k < MAX_CHUNKS; ++k) M = fmaxf(M, k < ncx ? mk[k] : -INFINITY);
-                float L = 0.f;
-#pragma unroll
-                for (int k = 0; k < MAX_CHUNKS; ++k) {
-                    w[k] = k < ncx ? ex2_approx(mk[k] - M) : 0.f;
-                    L = fmaf(w[k], lk[k], L);
-                }
-                const float inv_l = 1.f / L;
-#pragma unroll
-                for (int cb = 0; cb < 2; ++cb) {
-                    float acc[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-#pragma unroll
-                    for (int k0 = 0; k0 < MAX_CHUNKS; k0 += 4) {
-                        if (k0 < ncx) {
-                            float vals[4][32];
-#pragma unroll
-                            for (int kk = 0; kk < 4; ++kk) {
-                                const float *pc = base + (k0 + kk) * CH + (32 * cb) * BM;
-#pragma unroll
-                                for (int i = 0; i < 32; ++i) vals[kk][i] = 0.f;
-                                if (k0 + kk < ncx) {
-#pragma unroll
-                                    for (int i = 0; i < 32; ++i) vals[kk][i] = __ldcg(pc + i * BM);
-                                }
-                            }
-#pragma unroll
-                            for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-                                for (int i = 0; i < 32; ++i) acc[i] = fmaf(w[k0 + kk], vals[kk][i], acc[i]);
-                        }
-                    }
-                    uint32_t o[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = pack_half2(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
-                    put32(cb, o);
-                }
-                if (lane == 0) *cnt = 0u;  // re-armed for the next launch (every chunk has arrived)
-            }
+        if (kSplit) {  // split launches: these warps finish their own rows (A and B in parallel)
+            ok = split_epilogue(bars, p, tO, x, quarter, lane, row, it, g, m_used, l);
+            if (!ok) break;
+            continue;
         }
-        if (store) {
+        // The item's row statistics for the epilogue (double-buffered by item parity).
+        const int sb = kx & 1;
+        if (kx >= 2) {
+            ok = warp_wait(&bars->st_free[x][sb], ((kx >> 1) - 1) & 1, to);
+            if (!ok) break;
+        }
+        float *st = stats + (x * 2 + sb) * 2 * BM;
+        st[row] = m_used;
+        st[BM + row] = l;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->st_full[x][sb]);
+        ++kx;
+    }
+    if (!ok) raise_abort(bars, p.status, ST_PREFILL_SOFTMAX_TIMEOUT);
+}
+
+// ------------------------------------------------------------------ epilogue (4 warps, both tiles)
+// At the end of each item, for A then B: O / l -> fp16 -> this warp's output slot -> one TMA store of
+// its 32 rows (rows past T are clipped by the tensor map). A split unit first parks its unnormalised
+// rows in the workspace; the last chunk to arrive for 32 rows merges them.
+template <bool kSplit>
+__device__ void run_epilogue(uint8_t *smem, Bars *bars, const Params &p, const CUtensorMap *tm_att,
+                             uint32_t tbase, int warp, int lane) {
+    const unsigned long long to = p.timeout_ns;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t tl = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float *stats = reinterpret_cast<const float *>(smem + OFF_STATS);
+    uint8_t *slot = smem + OFF_OUT + quarter * OUT_SLOT;
+    // Row `lane` of the slot at lane * 128 B, 16-byte chunk k of a row at chunk position k ^ (row % 8)
+    // (the TMA 128-byte swizzle, which also makes these writes bank-conflict-free).
+    uint8_t *my_row = slot + lane * (HD * 2);
+    auto put16 = [&](int c16, const uint32_t(&o)[8]) {  // fp16 columns 16 c16 .. 16 c16 + 15 of this row
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int chunk = (2 * c16 + q) ^ (lane & 7);
+            *reinterpret_cast<uint4 *>(my_row + chunk * 16) =
+                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        }
+    };
+    if (kSplit) return;  // split launches: the softmax warps store their own rows
+    int kx[2] = {0, 0};  // items of each query tile so far
+    bool ok = true;
+    Item I;
+    for (int it = 0; ok && get_item<kSplit>(p, it, I); ++it) {
+        for (int x = 0; x < 2; ++x) {
+            if (I.nk_of(x) == 0) continue;
+            const int sb = kx[x] & 1;
+            ok = warp_wait(&bars->st[x].o_last, kx[x] & 1, to) &&
+                 warp_wait(&bars->st_full[x][sb], (kx[x] >> 1) & 1, to);
+            if (!ok) break;
+            ++kx[x];
+            tc_fence_after();
+            const float *st = stats + (x * 2 + sb) * 2 * BM;
+            const float l_row = st[BM + row];
+            const uint32_t tO = tl + TCOL_O + 64 * x;
+            // the slot's previous store has finished reading it (returns at once if none is pending)
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+            {
+                const float inv_l = 1.f / l_row;
+#pragma unroll
+                for (int c16 = 0; c16 < 4; ++c16) {  // 16 columns of O at a time (few registers)
+                    uint32_t v[16];
+                    tmem_ld16(tO + 16 * c16, v);
+                    tmem_wait_ld();
+                    uint32_t o[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        o[i] = pack_half2(__uint_as_float(v[2 * i]) * inv_l, __uint_as_float(v[2 * i + 1]) * inv_l);
+                    put16(c16, o);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {  // O and the statistics have been read
+                    mbar_arrive(&bars->st[x].o_free);
+                    mbar_arrive(&bars->st_free[x][sb]);
+                }
+            }
             fence_proxy_async_smem();  // this thread's slot writes -> visible to the TMA engine
             __syncwarp();
             const int row0 = (2 * I.pair + x) * BM + quarter * OUT_ROWS;
             if (lane == 0 && row0 < p.T) {  // rows past T inside the box are clipped by the tensor map
-                tma_store_3d(tm_att, smem + OFF_OUT + (x * 4 + quarter) * OUT_SLOT, I.h * HD, row0, I.b);
+                tma_store_3d(tm_att, slot, I.h * HD, row0, I.b);
                 bulk_commit_group();
             }
         }
@@ -743,7 +818,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     if (threadIdx.x == 0) {
         for (int s = 0; s < NQ; ++s) {
             mbar_init(&bars->q_full[s], 1);
-            mbar_init(&bars->q_empty[s], 2);
+            mbar_init(&bars->q_empty[s], 2);  // one release per query tile
         }
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&bars->k_full[s], 1);
@@ -756,10 +831,14 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
             mbar_init(&bars->st[x].s_free, NSOFT_WARPS);
             mbar_init(&bars->st[x].p_full, NSOFT_WARPS);
             mbar_init(&bars->st[x].o_done, 1);
-            mbar_init(&bars->st[x].o_free, NSOFT_WARPS);
-            mbar_init(&bars->st[x].drain, 1);
-            for (int q = 0; q < 4; ++q) bars->st[x].ex2_done[q] = 0;
+            mbar_init(&bars->st[x].o_last, 1);
+            mbar_init(&bars->st[x].o_free, 4);  // the epilogue warps
+            for (int s = 0; s < 2; ++s) {
+                mbar_init(&bars->st_full[x][s], NSOFT_WARPS);
+                mbar_init(&bars->st_free[x][s], 4);
+            }
         }
+        mbar_init(&bars->drain, 2);  // one commit from each MMA issuer
         bars->abort = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
@@ -775,7 +854,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
             tma_prefetch_l2_3d(&tm_qkv, 2 * p.E + i0.h * HD, i0.kv0 * BN, i0.b);
         }
     }
-    if (warp == 1) {
+    if (warp == MMA_WARP) {
         tmem_alloc(&bars->tmem_base, TMEM_COLS);
         tmem_relinquish();
     }
@@ -793,18 +872,25 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         reg_dealloc<WG0_REGS>();
         if (warp == 0) {
             if (lane == 0) run_producer<kSplit>(&tm_qkv, &tm_kv, smem, bars, p);
-        } else if (warp == 1 || warp == MMA_B_WARP) {
-            if (lane == 0) run_mma<kSplit>(smem, bars, p, tbase, warp == 1 ? 0 : 1);
+        } else if (warp == MMA_WARP || warp == MMA_B_WARP) {
+            run_mma<kSplit>(smem, bars, p, tbase, warp == MMA_WARP ? 0 : 1);
         }
         __syncwarp();
-    } else {  // WG1 / WG2: softmax of query tile A / B
+        // every MMA of both issuers has completed before TMEM is released (whole warp, converged)
+        if (warp == MMA_WARP && !warp_wait(&bars->drain, 0, p.timeout_ns) && lane == 0)
+            atomicOr(p.status, ST_PREFILL_DRAIN_TIMEOUT);
+        __syncwarp();
+    } else if (warp < EPI_WARP0) {  // WG1 / WG2: softmax of query tile A / B
         reg_alloc<SOFTMAX_REGS>();
-        run_softmax<kSplit>(smem, bars, p, &tm_att, tbase, (warp - SOFT_WARP0) / NSOFT_WARPS, warp, lane);
+        run_softmax<kSplit>(smem, bars, p, tbase, (warp - SOFT_WARP0) / NSOFT_WARPS, warp, lane);
+    } else {  // WG3: epilogue
+        reg_dealloc<EPI_REGS>();
+        run_epilogue<kSplit>(smem, bars, p, &tm_att, tbase, warp, lane);
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tbase, TMEM_COLS);
     }
@@ -978,6 +1064,8 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
 
     Params p;
     p.kv_fill = kv_layer != nullptr;
+    p.att = att;
+    p.att_seq_stride = att_seq_stride;
     p.T = T;
     auto magic = [](unsigned d, unsigned *m, int *l) {
         int sh = 0;

@@ -376,6 +376,18 @@ __device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
     return v;
 }
 
+// One lane of the (fully converged) warp is elected: true there, false on the other 31. Code that
+// runs on the whole warp and lets only the elected lane issue keeps its operands warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t e;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(e));
+    return e != 0;
+}
+
 // ---------------------------------------------------------------- per-warpgroup register budget
 // Executed by all 128 threads of a warpgroup: lowers / raises the registers each of its threads may
 // use. Raises wait until other warpgroups of the CTA have released enough, so a split must add up to
