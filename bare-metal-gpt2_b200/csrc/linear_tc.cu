@@ -146,51 +146,69 @@ __global__ void __launch_bounds__(NT, 1) k_linear_tc(const __grid_constant__ CUt
     // before it reads anything this grid writes).
     grid_launch_dependents();
 
-    if (warp == 0 && lane == 0) {
+    if (warp == 0) {
         // Producer: one W atom and one x atom per stage. The weights do not depend on the previous
         // kernel, so the first ring of W atoms is requested before waiting for it (programmatic
-        // dependent launch: this overlaps the previous kernel's tail); x follows the wait.
+        // dependent launch: this overlaps the previous kernel's tail); x follows the wait. The whole
+        // warp runs the loop (warp-uniform operands); one elected lane issues the copies.
+        const bool leader = elect_one();
         const int pre = min(na, p.nstage);
-        for (int i = 0; i < pre; ++i) {
-            mbar_arrive_expect_tx(&full[i], static_cast<uint32_t>(stage_bytes));
-            tma_load_2d(smem + i * stage_bytes, &tm_w, &full[i], (a0 + i) * KA, n0);
+        if (leader) {
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&full[i], static_cast<uint32_t>(stage_bytes));
+                tma_load_2d(smem + i * stage_bytes, &tm_w, &full[i], (a0 + i) * KA, n0);
+            }
         }
         grid_dependency_wait();
-        for (int i = 0; i < pre; ++i)
-            tma_load_2d(smem + i * stage_bytes + W_ATOM_BYTES, &tm_x, &full[i], (a0 + i) * KA, 0);
+        if (leader)
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(smem + i * stage_bytes + W_ATOM_BYTES, &tm_x, &full[i], (a0 + i) * KA, 0);
         for (int i = pre; i < na; ++i) {
             const int s = i % p.nstage;
-            if (!mbar_wait_spin(&empty[s], ((i / p.nstage) - 1) & 1, p.timeout_ns)) {
-                atomicOr(p.status, ST_LINEAR_TIMEOUT);
+            const bool ok = mbar_wait_spin(&empty[s], ((i / p.nstage) - 1) & 1, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (leader) atomicOr(p.status, ST_LINEAR_TIMEOUT);
                 break;
             }
-            uint8_t *st = smem + s * stage_bytes;
-            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
-            tma_load_2d(st, &tm_w, &full[s], (a0 + i) * KA, n0);
-            tma_load_2d(st + W_ATOM_BYTES, &tm_x, &full[s], (a0 + i) * KA, 0);
+            if (leader) {
+                uint8_t *st = smem + s * stage_bytes;
+                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
+                tma_load_2d(st, &tm_w, &full[s], (a0 + i) * KA, n0);
+                tma_load_2d(st + W_ATOM_BYTES, &tm_x, &full[s], (a0 + i) * KA, 0);
+            }
+            __syncwarp();
         }
     } else {
         grid_dependency_wait();
     }
-    if (warp == 1 && lane == 0) {
-        // MMA issuer.
+    if (warp == 1) {
+        // MMA issuer: the whole warp waits (warp-uniform descriptors, kept in uniform registers);
+        // one elected lane issues. Descriptors are built once and advanced by 32-bit adds.
+        const bool leader = elect_one();
         const uint32_t idesc = idesc_f16_f32(BM, p.bpad, 0, 0);
+        const uint64_t dw0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+        const uint64_t dx0 = sdesc_sw128(smem_u32(smem + W_ATOM_BYTES), 16, 1024);
+        const uint32_t w_lo = static_cast<uint32_t>(dw0), w_hi = static_cast<uint32_t>(dw0 >> 32);
+        const uint32_t x_lo = static_cast<uint32_t>(dx0), x_hi = static_cast<uint32_t>(dx0 >> 32);
         for (int i = 0; i < na; ++i) {
             const int s = i % p.nstage;
-            if (!mbar_wait_spin(&full[s], (i / p.nstage) & 1, p.timeout_ns)) {
-                atomicOr(p.status, ST_LINEAR_TIMEOUT);
+            const bool ok = mbar_wait_spin(&full[s], (i / p.nstage) & 1, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (leader) atomicOr(p.status, ST_LINEAR_TIMEOUT);
                 break;
             }
             tc_fence_after();
-            const uint32_t wa = smem_u32(smem + s * stage_bytes);
-            const uint64_t dw = sdesc_sw128(wa, 16, 1024);
-            const uint64_t dx = sdesc_sw128(wa + W_ATOM_BYTES, 16, 1024);
+            const uint32_t off = static_cast<uint32_t>((s * stage_bytes) >> 4);
+            if (leader) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                umma_f16_ss(tbase, dw + 2 * kk, dx + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(&empty[s]);
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_f16_ss_lohi(tbase, w_lo + off + 2 * kk, w_hi, x_lo + off + 2 * kk, x_hi, idesc,
+                                     (i > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            __syncwarp();
         }
-        umma_commit(done);  // arrives once every MMA issued above has completed
+        if (leader) umma_commit(done);  // arrives once every MMA issued above has completed
     }
     __syncwarp();
 
