@@ -144,9 +144,12 @@ class HostGather:
         self.array = np.memmap(self.path, dtype=dtype, mode="r+", shape=tuple(shape))
         self.tensor = torch.from_numpy(self.array)
         self.registered = False
+        self.register_error = None
         if torch.cuda.is_available():
             rc = torch.cuda.cudart().cudaHostRegister(self.tensor.data_ptr(), nbytes, 0)
             self.registered = int(rc) == 0
+            if not self.registered:
+                self.register_error = f"{rc} ({int(rc)})"
 
     def rows(self, lo: int, hi: int):
         return self.tensor[lo:hi]
@@ -540,6 +543,7 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
     launches = lib.gpt2_b200_batch_launches_per_step(h, 0)
     lib.gpt2_b200_batch_destroy(h)
     status = lib.status()
+    pinned = gather.registered  # (close() unregisters the buffer)
     gather.close()
     rows = range(total_seqs) if rank == 0 else range(lo, hi)  # rank 0 checks the whole gather
     prompts_kept = all(np.array_equal(tokens[r, :plen_all[r]], prompt_all[r, :plen_all[r]]) for r in rows)
@@ -560,7 +564,7 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
             "h2d_bytes": int(h_prompt.numel() * 4 + h_plen.numel() * 4),
             "d2h_bytes": int(h_out.numel() * 4),
             "output_gather": "each rank D2H into its rows of one shared page-locked host buffer"
-                             + ("" if gather.registered else " (unregistered)")}
+                             + ("" if pinned else f" (not page-locked: {gather.register_error})")}
 
 
 # ---------------------------------------------------------------------------------------- CPU legs
