@@ -260,7 +260,7 @@ def host_seconds_per_step(torch, enqueue, n):
     return dt / max(1, n)
 
 
-def timed_region(torch, stream, steps, enqueue, host_step_s):
+def timed_region(torch, stream, steps, enqueue, host_step_s, finish=None):
     """Device time of `steps` back-to-back steps: one CUDA event pair around the whole region, on the
     launching stream. Before the start event the stream is held by torch.cuda._sleep (a busy loop of a
     fixed number of clock cycles, outside the region) long enough for the host to enqueue every step,
@@ -277,6 +277,8 @@ def timed_region(torch, stream, steps, enqueue, host_step_s):
     t0 = time.perf_counter()
     for i in range(steps):
         enqueue(i)
+    if finish is not None:
+        finish()  # joins any side streams back into `stream` before the end event
     enq_s = time.perf_counter() - t0
     end.record(stream)
     torch.cuda.synchronize()
@@ -413,12 +415,14 @@ def bench_decode_batched(torch, lib, steps, warmup, world, rank, ctx, seed, tota
             "host_kept_ahead": ahead}
 
 
-def bench_e2e_prefill(torch, lib, steps, warmup, seed, nstreams=3):
+def bench_e2e_prefill(torch, lib, steps, warmup, seed, nstreams=6):
     """End to end through the reference-facing C ABI with host buffers: per layer, pinned host qkv ->
     device (cudaMemcpyAsync), gpt2_attention_b200_stream (the reference's GPT2Backend.attention slot,
     with a stream), att -> pinned host. Layers rotate over `nstreams` streams, each with its own
     one-layer device buffers, so one layer's upload, another's attention and a third's download
-    overlap. The step ends when every layer's output is back in host memory."""
+    overlap; consecutive steps pipeline the same way (a step's uploads start while the previous
+    step's last layers finish), and the streams are joined once, at the end of the timed region. Every
+    step still moves all of its inputs host -> device and all of its outputs device -> host."""
     main = torch.cuda.current_stream()
     streams = [torch.cuda.Stream() for _ in range(nstreams)]
     host_in = [seeded_fp16(torch, (LAYERS, P, QKV), seed + i, "cpu").pin_memory() for i in range(2)]
@@ -428,11 +432,13 @@ def bench_e2e_prefill(torch, lib, steps, warmup, seed, nstreams=3):
     start_ev = torch.cuda.Event()
 
     def step(i):
-        start_ev.record(main)
+        if i == 0:  # the side streams start after whatever `main` holds (the timed region's start)
+            start_ev.record(main)
+            for st in streams:
+                st.wait_event(start_ev)
         for L in range(LAYERS):
-            k = L % nstreams
+            k = (i * LAYERS + L) % nstreams
             st = streams[k]
-            st.wait_event(start_ev)
             with torch.cuda.stream(st):
                 d_in[k].copy_(host_in[i % 2][L], non_blocking=True)
                 rc = lib.gpt2_attention_b200_stream(d_out[k].data_ptr(), d_in[k].data_ptr(), P, E, H, D,
@@ -440,11 +446,17 @@ def bench_e2e_prefill(torch, lib, steps, warmup, seed, nstreams=3):
                 if rc != 0:
                     raise RuntimeError(f"e2e attention failed: {lib.gpt2_b200_strerror(rc).decode()}")
                 host_out[L].copy_(d_out[k], non_blocking=True)
+
+    def join():
         for st in streams:
             main.wait_stream(st)
 
-    host_s = host_seconds_per_step(torch, step, max(2, warmup))
-    region, ahead = timed_region(torch, main, steps, step, host_s)
+    def step_joined(i):  # host enqueue cost measured per step, joined so the warm-up drains
+        step(i)
+        join()
+
+    host_s = host_seconds_per_step(torch, step_joined, max(2, warmup))
+    region, ahead = timed_region(torch, main, steps, step, host_s, finish=join)
     ms = region / steps
     return {"ms_per_step": ms, "h2d": LAYERS * P * QKV * 2, "d2h": LAYERS * P * E * 2,
             "host_kept_ahead": ahead, "streams": nstreams}
