@@ -297,7 +297,6 @@ unsigned gpt2_b200_status(int clear) {
         cudaMemset(ctx->status, 0, sizeof(unsigned));
         // A kernel that gave up may have left split-merge arrival counters part-way: re-arm them.
         if (ctx->counters) cudaMemset(ctx->counters, 0, ctx->counter_words * sizeof(unsigned));
-        if (ctx->pf_counters) cudaMemset(ctx->pf_counters, 0, ctx->pf_counter_words * sizeof(unsigned));
         cudaDeviceSynchronize();
     }
     return v;

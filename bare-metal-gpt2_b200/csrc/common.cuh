@@ -35,10 +35,7 @@ struct DeviceContext {
     unsigned *counters = nullptr;   // decode split-arrival counters (kept at zero between calls)
     size_t part_floats = 0;
     size_t counter_words = 0;
-    float *pf_part = nullptr;       // prefill: partial rows of split work units
-    unsigned *pf_counters = nullptr;  // prefill: chunk arrivals per 32 rows (kept at zero)
-    size_t pf_part_floats = 0;
-    size_t pf_counter_words = 0;
+    int pf_active_clusters[5] = {0, 0, 0, 0, 0};  // prefill split clusters of n CTAs that fit (0 = not asked)
     bool prefill_attr_done = false;
     bool decode_attr_done = false;
     int num_sms = 0;

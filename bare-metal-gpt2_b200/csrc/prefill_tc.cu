@@ -12,50 +12,55 @@
 // snake order), with TMEM and barriers set up once.
 //
 // The work of a CTA is a sequence of UNITS, one query tile against one K/V tile, in the order
-// item by item, K/V tile by K/V tile, A before B. For head_dim 64 a unit's 16,384 exponentials cost
-// each SM sub-partition 1,024 cycles of its MUFU (ex2) pipe against ~680 tensor cycles for the unit's
-// two MMAs (QK at full rate, PV with N = 64 at ~60 %), so the kernel is built to keep the MUFU pipes
-// busy: softmax warps never wait for anything but their next S, and two softmax warps share each
+// item by item, K/V tile by K/V tile. For head_dim 64 a unit's 16,384 exponentials cost each SM
+// sub-partition 1,024 cycles of its MUFU (ex2) pipe against ~680 tensor cycles for the unit's two
+// MMAs (QK at full rate, PV with N = 64 at ~60 %), so the kernel is built to keep the MUFU pipes busy:
+// softmax warps never wait for anything but their next S, and two softmax warps share each
 // sub-partition, their exponential phases overlapping (one warp alone issues ex2 at ~75 % of the
 // pipe's rate, two reach ~90 %). Roles (16 warps, 4 warpgroups):
 //
 //   warp 0   (1 thread)  TMA producer: the two Q tiles of each item (double-buffered), then K(t) and
 //                        V(t-1) tiles (128 x 64 fp16, 128-byte swizzle) straight out of the packed qkv
 //                        rows into 4-stage K and V rings, running ahead across item boundaries.
-//   warps 2, 1           MMA issuers for both query tiles, in unit order. Warp 2: S_u = Q K^T into one of
-//                        three TMEM S buffers (M128 N128 K64, 4 x tcgen05.mma K16), issued as soon as
-//                        the PV of unit u-3 (the buffer's previous user) has completed. Warp 1: O_x +=
-//                        P_u V (M128 N64 K128, 8 x tcgen05.mma K16, P read from TMEM) once the softmax
-//                        has written P_u.
+//   warps 1, 2           MMA issuers of query tile A, of B, each on its whole warp with one elected
+//                        lane: S_x = Q_x K^T (M128 N128 K64, 4 x tcgen05.mma K16) once the softmax has
+//                        read the previous S_x, O_x += P_x V (M128 N64 K128, 8 x K16, P read from
+//                        TMEM) once it has written P_x.
 //   warps 4-7, 8-11      softmax of query tile A, of B: one thread per query row (TMEM lane), all 128
 //                        scores of a unit in registers. Log2 domain (1/8 * log2(e) folded into one
-//                        FFMA, hardware ex2); causal mask on the diagonal tile only; P = 2^(s-m) written
-//                        as packed fp16 over the first 64 columns of the unit's own S buffer; the row
-//                        sum adds the fp16-rounded P values (numerator and denominator use identical
-//                        weights); O is rescaled in TMEM only when the running max grows by more than
-//                        2^8 (the stale max is otherwise kept for both l and O: exact, and P <= 256).
+//                        FFMA, hardware ex2); causal mask on the diagonal tile only; P = 2^(s-m) as
+//                        packed fp16 kept in registers until the previous PV has completed, then
+//                        written to the tile's P columns; the row sum adds the fp16-rounded P values
+//                        (numerator and denominator use identical weights); O is rescaled in TMEM only
+//                        when the running max grows by more than 2^8 (the stale max is otherwise kept
+//                        for both l and O: exact, and P <= 256).
 //   warps 12-15          epilogue of both query tiles: at the end of an item, O / l -> fp16 -> a
 //                        swizzled 4 KB shared-memory slot per warp -> one TMA store of the warp's 32
-//                        rows, so output rows leave as whole 128-byte lines; the split path's partial
-//                        rows and merge (below) also run here.
+//                        rows, so output rows leave as whole 128-byte lines.
 //
-// Launches with fewer whole pairs than SMs (one layer of one sequence) run the kSplit instantiation: a
-// work unit is a chunk of a pair's key range; split units park unnormalised rows (o, m, l) in a
-// workspace and the last chunk to arrive for a 32-row group merges them. With a KV-cache target the
-// producer also stores the K/V tiles its unit owns into the cache, straight from the ring.
+// Launches with fewer whole pairs than SMs (one layer of one sequence) run the kSplit instantiation:
+// a work unit is a chunk of a pair's key range, one unit per CTA, and the chunks of a pair run in one
+// thread-block cluster (up to 4 CTAs, placed by the host). At the end of its unit each softmax warp
+// of a chunk pushes its 32 unnormalised rows (o, m, l) into the shared memory of the CTA that merges
+// those rows (remote st.async stores that complete on an mbarrier there); the merging warp combines
+// them with its own rows and stores the output, so no partial row goes through global memory. With a
+// KV-cache target the producer also stores the K/V tiles its unit owns into the cache, straight from
+// the ring.
 //
-// TMEM: all 512 columns (S buffers at 0, 128, 256; O_A 384, O_B 448). Shared memory: Q 64 KB, K and V
-// rings 128 KB, output slots 16 KB, row statistics 4 KB, barriers. No cluster, no multicast. Every
-// mbarrier wait is bounded. Registers: the launch gives each of the 512 threads 128; the producer /
-// MMA warpgroup and the epilogue warpgroup hand some back (setmaxnreg) so that the softmax warps hold
-// their 128 scores without spilling.
+// TMEM: all 512 columns (S_A at 0, S_B at 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory:
+// Q 64 KB, K and V rings 128 KB, output slots 16 KB, row statistics 4 KB (split launches receive the
+// pushed partial rows there instead), barriers. No multicast. Every mbarrier wait is bounded.
+// Registers: the launch gives each of the 512 threads 128; the producer / MMA warpgroup and the
+// epilogue warpgroup hand some back (setmaxnreg) so that the softmax warps hold their 128 scores
+// without spilling.
 //
 // Launch: a programmatic dependent of the previous kernel in the stream. Barrier init, TMEM
 // allocation and an L2 prefetch of the first item's Q, K and V tiles overlap that kernel's tail;
-// every load, store and workspace access follows the grid dependency wait.
+// every global load and store follows the grid dependency wait.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <type_traits>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -79,6 +84,17 @@ constexpr int OFF_STATS = OFF_OUT + 4 * OUT_SLOT;     // [2 tiles][2 item pariti
 constexpr int OFF_BAR = OFF_STATS + 2 * 2 * 2 * BM * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+// Split launches: a softmax warp's 32 partial rows as pushed to the merging CTA: o as [16 column
+// quads][32 rows] float4 (conflict-free for one row per lane on both sides), then (m, l) per row.
+constexpr int MAX_CLUSTER = 4;  // chunks of one pair at most (= CTAs of a cluster)
+constexpr int PART_O_BYTES = (HD / 4) * 32 * 16;
+constexpr int PART_BYTES = PART_O_BYTES + 32 * 8;
+// A split CTA has one unit, so it never uses the second Q buffer, the output slots and statistics,
+// nor the K stages past its unit's K/V tiles: the pushed partials land there (see recv_slot).
+constexpr int RECV_Q_SLOTS = 2 * TILE_BYTES / PART_BYTES;                   // 3
+constexpr int RECV_OUT_SLOTS = (OFF_BAR - OFF_OUT) / PART_BYTES;            // 2
+static_assert(RECV_Q_SLOTS == 3 && RECV_OUT_SLOTS == 2, "receive slots");
+constexpr int MAX_SPLIT_CTAS = 160;  // CTAs of a split launch at most (one unit each, <= the SM count)
 constexpr int NSOFT_WARPS = 4;  // per query tile: one warp per TMEM lane quarter
 // Four warpgroups, one warp of each on every SM sub-partition: WG0 = warps 0-3 (producer, the two MMA
 // issuers, one idle warp), WG1 = softmax of A, WG2 = softmax of B, WG3 = epilogue. The launch gives every
@@ -125,6 +141,7 @@ struct __align__(8) Bars {
     uint64_t st_full[2][2];    // softmax of tile x wrote its item's row statistics (buffer = item parity)
     uint64_t st_free[2][2];    // the epilogue has read them
     uint64_t drain;            // teardown: every MMA of both issuers has completed
+    uint64_t recv[2][4];       // split launches: the pushed partial rows of [query tile][lane quarter]
     uint32_t tmem_base;
     int abort;
 };
@@ -138,19 +155,24 @@ struct Params {
     int n_pairs;               // ceil(n_qtiles / 2)
     int kv_chunk;              // K/V tiles per work unit (>= n_qtiles: a pair is never split)
     int units_per_hb;          // work units per (head, sequence): sum over pairs of their chunks
-    int max_chunks;            // chunks of the longest pair (partial-row slots per query tile)
     int total_items;           // units_per_hb * H * B
     float scale_log2;          // log2(e) / sqrt(D)
-    float *part;               // split units: partials [group][chunk][PART_COLS][128 rows]
     int kv_fill;               // also write K/V rows 0..T-1 into a KV-cache layer (B == 1)
-    unsigned *counters;        // split units: arrivals per [group][lane quarter], re-armed to 0
     unsigned *status;
     unsigned long long timeout_ns;
     __half *att;               // split launches: output rows are stored directly (no TMA slot)
     long long att_seq_stride;  // elements between sequences of att
 };
-constexpr int PART_COLS = HD + 2;  // o[64], m, l of a row; stored column-major (coalesced)
-constexpr int MAX_CHUNKS = 8;       // chunks per pair at most (the merge is unrolled over them)
+
+// Split launches: the work unit (item number) of each CTA, -1 for none. The host places the chunks of
+// a pair in one cluster, chunk k at cluster rank (rank of chunk 0) + k. A separate kernel argument,
+// absent (empty) from whole-pair launches.
+struct SplitTable {
+    short cta_item[MAX_SPLIT_CTAS];
+};
+struct NoSplitTable {};
+template <bool kSplit>
+using SplitArg = typename std::conditional<kSplit, SplitTable, NoSplitTable>::type;
 
 struct Item {
     int pair, h, b;
@@ -176,17 +198,40 @@ __device__ __forceinline__ int pair_kv_tiles(const Params &p, int pair) {
     return (2 * pair + 1 < p.n_qtiles) ? 2 * pair + 2 : 2 * pair + 1;
 }
 
+// Shared-memory offset of receive slot i of a split CTA whose unit loads at most kv_chunk K/V tiles.
+__device__ __forceinline__ uint32_t recv_slot(int i, int kv_chunk) {
+    if (i < RECV_Q_SLOTS) return OFF_Q + 2 * TILE_BYTES + i * PART_BYTES;
+    if (i < RECV_Q_SLOTS + RECV_OUT_SLOTS) return OFF_OUT + (i - RECV_Q_SLOTS) * PART_BYTES;
+    return OFF_K + kv_chunk * TILE_BYTES + (i - RECV_Q_SLOTS - RECV_OUT_SLOTS) * PART_BYTES;
+}
+
+// Chunks of a pair holding keys of its query tile x (its keys are K/V tiles 0 .. 2 pair + x: the
+// first chunks), 0 when the tile is past T.
+__device__ __forceinline__ int tile_chunks(const Params &p, int pair, int x) {
+    return (2 * pair + x < p.n_qtiles) ? (2 * pair + x + p.kv_chunk) / p.kv_chunk : 0;
+}
+
+// Split launches: this CTA's unit (SplitTable::cta_item[blockIdx.x]), read once by thread 0 at launch.
+__shared__ int s_split_item;
+
 // The r-th work unit of this CTA. A unit is one chunk of kv_chunk K/V tiles of a pair of query tiles
 // (the whole key range unless the launch is too small to fill the SMs with whole pairs). Units are
 // numbered heaviest pair first; rounds alternate direction (snake) so that each CTA gets a mix of
 // heavy and light units. Returns false when this CTA has no r-th unit (nor any later one).
 template <bool kSplit>
 __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
-    const int G = gridDim.x, c = blockIdx.x;
-    const long long i = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - c) : c);
-    if (i >= p.total_items) return false;
+    int idx;
+    if (kSplit) {  // one unit per CTA, placed by the host
+        if (r > 0) return false;
+        idx = s_split_item;
+        if (idx < 0) return false;
+    } else {
+        const int G = gridDim.x, c = blockIdx.x;
+        const long long i = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - c) : c);
+        if (i >= p.total_items) return false;
+        idx = static_cast<int>(i);
+    }
     const int per = p.H * p.B;
-    const int idx = static_cast<int>(i);
     int u = static_cast<int>(div_magic(idx, per, p.hb_magic, p.hb_shift));  // unit in its (head, seq)
     const int rem = idx - u * per;
     it.b = static_cast<int>(div_magic(rem, p.H, p.h_magic, p.h_shift));
@@ -309,10 +354,11 @@ __device__ void run_producer(const CUtensorMap *tm, const CUtensorMap *tm_kv, ui
                     (kc.I.kv0 + kc.j) * BN, kc.I.b);
         last_k[s] = kc.g;
         own_k[s] = owned(kc);
-        // Launch: every CTA asks for its first Q and K(0) alone, and only then for the rest of the
-        // rings, so the first QK does not queue behind ~24 MB of later tiles requested by all SMs
-        // at once (measured -2..3 % at P=1024).
-        if (kc.g == 0 && !(ok = mbar_wait(&bars->k_full[0], 0, to))) break;
+        // Launch: every CTA of a whole-pair launch asks for its first Q and K(0) alone, and only then
+        // for the rest of the rings, so the first QK does not queue behind ~24 MB of later tiles
+        // requested by all SMs at once (measured -2..3 % at P=1024). A split unit has only a few
+        // tiles: it asks for all of them at once.
+        if (!kSplit && kc.g == 0 && !(ok = mbar_wait(&bars->k_full[0], 0, to))) break;
         kc.advance(p);
         if (vc.g + 1 < kc.g && !(ok = load_v())) break;  // V one tile behind K
     }
@@ -467,127 +513,112 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
 
 // ------------------------------------------------------------------ softmax
 
-// End of an item in a split launch, run by the item's softmax warps (32 rows each): once the item's
-// last PV of this query tile has completed, O / l goes straight to att when the item is a whole pair;
-// a chunk of a pair parks its unnormalised rows (o, m, l) in the workspace and the last chunk to
-// arrive for these 32 rows merges every chunk's partial. Rows are stored as whole 128-byte lines.
-// Returns false when a wait expired.
-__device__ __forceinline__ bool split_epilogue(Bars *bars, const Params &p, uint32_t tO, int x, int quarter,
-                                            int lane, int row, int it, int g, float m_row, float l_row) {
-    Stream &S = bars->st[x];
-    if (!warp_wait(&S.o_done, (g - 1) & 1, p.timeout_ns)) return false;  // the item's last PV
-    tc_fence_after();
-    Item I;
-    get_item<true>(p, it, I);
-    const int qrow = (2 * I.pair + x) * BM + row;  // query index of this thread's row
-    uint4 *dst = reinterpret_cast<uint4 *>(p.att + I.b * p.att_seq_stride +
-                                           static_cast<long long>(qrow) * p.E + I.h * HD);
-    auto store_row = [&](const float (&o)[32], int half) {  // 32 columns of this row, normalised
-        if (qrow < p.T) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                dst[4 * half + q] = make_uint4(pack_half2(o[8 * q], o[8 * q + 1]), pack_half2(o[8 * q + 2], o[8 * q + 3]),
-                                               pack_half2(o[8 * q + 4], o[8 * q + 5]), pack_half2(o[8 * q + 6], o[8 * q + 7]));
-        }
-    };
-    if (I.nchunk == 1) {
-        const float inv_l = 1.f / l_row;
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            uint32_t v[32];
-            tmem_ld32(tO + 32 * cb, v);
-            tmem_wait_ld();
-            float o[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]) * inv_l;
-            store_row(o, cb);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.o_free);
-        return true;
+// The 32-row groups of a pair in a split launch: g = 4 x + lane quarter. Group g is merged by chunk
+// g % nc (nc = chunks holding query tile x's keys), which receives the other nc - 1 chunks' partial
+// rows of g in consecutive slots after those of the groups it merges before g.
+__device__ __forceinline__ int merge_first_slot(const Params &p, int pair, int g, int km) {
+    int slot = 0;
+    for (int g2 = 0; g2 < g; ++g2) {
+        const int n2 = tile_chunks(p, pair, g2 >> 2);
+        if (n2 > 1 && g2 % n2 == km) slot += n2 - 1;
     }
-    const long long grp = ((static_cast<long long>(I.b) * p.H + I.h) * p.n_pairs + I.pair) * 2 + x;
-    // column c of this row of chunk k at part[((grp * max_chunks + k) * PART_COLS + c) * 128 + row]
-    float *mine = p.part + (grp * p.max_chunks + I.chunk) * (PART_COLS * BM) + row;
-#pragma unroll
-    for (int cb = 0; cb < 2; ++cb) {
-        uint32_t v[32];
-        tmem_ld32(tO + 32 * cb, v);
+    return slot;
+}
+
+// End of the unit of a split launch, run by each softmax warp for its 32 rows once the unit's last PV
+// of its query tile has completed. Rows whose keys all lie in this chunk are normalised and stored;
+// otherwise a chunk that does not merge these rows pushes its unnormalised rows (o, m, l) into the
+// merging CTA (st.async, completing on that CTA's receive barrier), and the merging warp waits for
+// the other chunks' rows, combines them with its own and stores the result. Output rows leave as
+// whole 128-byte lines. Returns false when a wait expired.
+__device__ __forceinline__ bool split_epilogue(uint8_t *smem, Bars *bars, const Params &p, const Item &I,
+                                            uint32_t tO, int x, int quarter, int lane, int row, int g,
+                                            float m_row, float l_row) {
+    Stream &S = bars->st[x];
+    if (!warp_wait(&S.o_done, (g - 1) & 1, p.timeout_ns)) return false;  // the unit's last PV
+    tc_fence_after();
+    float o[HD];
+    {
+        uint32_t v[2][32];
+        tmem_ld32(tO, v[0]);
+        tmem_ld32(tO + 32, v[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) __stcg(mine + (32 * cb + i) * BM, __uint_as_float(v[i]));
+        for (int i = 0; i < HD; ++i) o[i] = __uint_as_float(v[i >> 5][i & 31]);
     }
-    __stcg(mine + HD * BM, m_row);
-    __stcg(mine + (HD + 1) * BM, l_row);
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&S.o_free);  // the next item's first PV may overwrite O
-    // Publish the warp's 32 partial rows and count this chunk's arrival in one release-acquire atomic
-    // (the warp barrier orders every lane's stores before lane 0's release; the last arrival's acquire
-    // makes every chunk's rows visible to the merge below).
-    unsigned *cnt = p.counters + grp * 4 + quarter;
-    const int ncx = (2 * I.pair + x + p.kv_chunk) / p.kv_chunk;  // chunks with this tile's keys
-    unsigned prev = 0;
-    if (lane == 0)
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != static_cast<unsigned>(ncx - 1)) return true;
-    // last chunk of these 32 rows: merge every chunk's partial row
-    const float *base = p.part + grp * p.max_chunks * (PART_COLS * BM) + row;
-    constexpr int CH = PART_COLS * BM;  // floats per chunk
-    // Loads are predicated rather than branched so that each batch is one L2 round trip: (m, l) of
-    // every chunk, then per 32-column half up to 4 chunks' values at once.
-    float mk[MAX_CHUNKS], lk[MAX_CHUNKS], w[MAX_CHUNKS];
+    if (lane == 0) mbar_arrive(&S.o_free);
+    const int ncx = tile_chunks(p, I.pair, x);
+    const int grp = 4 * x + quarter;
+    const int km = ncx > 1 ? grp % ncx : I.chunk;  // the chunk that merges these rows
+    if (I.chunk != km) {  // push this chunk's rows to the merging CTA (the same slots of its space)
+        const int slot = merge_first_slot(p, I.pair, grp, km) + (I.chunk < km ? I.chunk : I.chunk - 1);
+        const uint32_t rank = cluster_rank() - static_cast<uint32_t>(I.chunk) + static_cast<uint32_t>(km);
+        const uint32_t dst = dsmem_addr(smem_u32(smem + recv_slot(slot, p.kv_chunk)), rank);
+        const uint32_t bar = dsmem_addr(smem_u32(&bars->recv[x][quarter]), rank);
 #pragma unroll
-    for (int k = 0; k < MAX_CHUNKS; ++k) {
-        mk[k] = -INFINITY;
-        lk[k] = 0.f;
-        if (k < ncx) {
-            mk[k] = __ldcg(base + k * CH + HD * BM);
-            lk[k] = __ldcg(base + k * CH + (HD + 1) * BM);
-        }
+        for (int c4 = 0; c4 < HD / 4; ++c4)
+            st_async_v4(dst + (c4 * 32 + lane) * 16, make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]),
+                        bar);
+        st_async_v2(dst + PART_O_BYTES + lane * 8, m_row, l_row, bar);
+        return true;
     }
-    float M = -INFINITY;
+    float inv_l;
+    if (ncx > 1) {  // merge the other chunks' rows into this one's
+        if (!warp_wait(&bars->recv[x][quarter], 0, p.timeout_ns)) return false;
+        const int s0 = merge_first_slot(p, I.pair, grp, km);
+        const uint32_t in0 = smem_u32(smem) + static_cast<uint32_t>(lane) * 16u;
+        float mk[MAX_CLUSTER - 1], lk[MAX_CLUSTER - 1];
+        float M = m_row;
 #pragma unroll
-    for (int k = 0; k < MAX_CHUNKS; ++k) M = fmaxf(M, k < ncx ? mk[k] : -INFINITY);
-    float L = 0.f;
-#pragma unroll
-    for (int k = 0; k < MAX_CHUNKS; ++k) {
-        w[k] = k < ncx ? ex2_approx(mk[k] - M) : 0.f;
-        L = fmaf(w[k], lk[k], L);
-    }
-    const float inv_l = 1.f / L;
-#pragma unroll
-    for (int cb = 0; cb < 2; ++cb) {
-        float acc[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-#pragma unroll
-        for (int k0 = 0; k0 < MAX_CHUNKS; k0 += 4) {
-            if (k0 < ncx) {
-                float vals[4][32];
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const float *pc = base + (k0 + kk) * CH + (32 * cb) * BM;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) vals[kk][i] = 0.f;
-                    if (k0 + kk < ncx) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) vals[kk][i] = __ldcg(pc + i * BM);
-                    }
-                }
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[i] = fmaf(w[k0 + kk], vals[kk][i], acc[i]);
+        for (int k = 0; k < MAX_CLUSTER - 1; ++k) {
+            mk[k] = -INFINITY;
+            lk[k] = 0.f;
+            if (k < ncx - 1) {
+                const float2 ml = lds_v2(smem_u32(smem) + recv_slot(s0 + k, p.kv_chunk) + PART_O_BYTES + lane * 8);
+                mk[k] = ml.x;
+                lk[k] = ml.y;
+                M = fmaxf(M, ml.x);
             }
         }
+        const float ws = ex2_approx(m_row - M);
+        float L = ws * l_row;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] *= inv_l;
-        store_row(acc, cb);
+        for (int i = 0; i < HD; ++i) o[i] *= ws;
+#pragma unroll
+        for (int k = 0; k < MAX_CLUSTER - 1; ++k) {
+            if (k < ncx - 1) {
+                const float w = ex2_approx(mk[k] - M);
+                L = fmaf(w, lk[k], L);
+                const uint32_t in = in0 + recv_slot(s0 + k, p.kv_chunk);
+                float4 q[HD / 4];  // the whole partial row first: one round of shared-memory latency
+#pragma unroll
+                for (int c4 = 0; c4 < HD / 4; ++c4) q[c4] = lds_v4(in + c4 * 512);
+#pragma unroll
+                for (int c4 = 0; c4 < HD / 4; ++c4) {
+                    o[4 * c4] = fmaf(w, q[c4].x, o[4 * c4]);
+                    o[4 * c4 + 1] = fmaf(w, q[c4].y, o[4 * c4 + 1]);
+                    o[4 * c4 + 2] = fmaf(w, q[c4].z, o[4 * c4 + 2]);
+                    o[4 * c4 + 3] = fmaf(w, q[c4].w, o[4 * c4 + 3]);
+                }
+            }
+        }
+        inv_l = 1.f / L;
+    } else {
+        inv_l = 1.f / l_row;
     }
-    if (lane == 0) *cnt = 0u;  // re-armed for the next launch (every chunk has arrived)
+    const int qrow = (2 * I.pair + x) * BM + row;  // query index of this thread's row
+    if (qrow < p.T) {
+        uint4 *dst = reinterpret_cast<uint4 *>(p.att + I.b * p.att_seq_stride + static_cast<long long>(qrow) * p.E +
+                                               I.h * HD);
+#pragma unroll
+        for (int q = 0; q < HD / 8; ++q)
+            dst[q] = make_uint4(pack_half2(o[8 * q] * inv_l, o[8 * q + 1] * inv_l),
+                                pack_half2(o[8 * q + 2] * inv_l, o[8 * q + 3] * inv_l),
+                                pack_half2(o[8 * q + 4] * inv_l, o[8 * q + 5] * inv_l),
+                                pack_half2(o[8 * q + 6] * inv_l, o[8 * q + 7] * inv_l));
+    }
     return true;
 }
 
@@ -613,6 +644,9 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
     int g = 0;   // this query tile's K/V tiles processed so far (all items)
     int kx = 0;  // items in which this query tile has keys (statistics buffer)
     bool ok = true;
+    // Split launches: every peer of the cluster has initialised its receive barriers (the cluster
+    // barrier's arrival follows the set-up of every CTA) before this warp pushes into one.
+    if (kSplit) cluster_wait();
     Item I;
     for (int it = 0; ok && get_item<kSplit>(p, it, I); ++it) {
         const int nk = I.nk_of(x);
@@ -704,7 +738,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
         }
         if (!ok) break;
         if (kSplit) {  // split launches: these warps finish their own rows (A and B in parallel)
-            ok = split_epilogue(bars, p, tO, x, quarter, lane, row, it, g, m_used, l);
+            ok = split_epilogue(smem, bars, p, I, tO, x, quarter, lane, row, g, m_used, l);
             if (!ok) break;
             continue;
         }
@@ -726,8 +760,7 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
 
 // ------------------------------------------------------------------ epilogue (4 warps, both tiles)
 // At the end of each item, for A then B: O / l -> fp16 -> this warp's output slot -> one TMA store of
-// its 32 rows (rows past T are clipped by the tensor map). A split unit first parks its unnormalised
-// rows in the workspace; the last chunk to arrive for 32 rows merges them.
+// its 32 rows (rows past T are clipped by the tensor map). Split launches do not use these warps.
 template <bool kSplit>
 __device__ void run_epilogue(uint8_t *smem, Bars *bars, const Params &p, const CUtensorMap *tm_att,
                              uint32_t tbase, int warp, int lane) {
@@ -806,13 +839,24 @@ __device__ void run_epilogue(uint8_t *smem, Bars *bars, const Params &p, const C
 template <bool kSplit>
 __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     k_flash_prefill_tc(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_att,
-                       const __grid_constant__ CUtensorMap tm_kv, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_kv, const Params p, const SplitArg<kSplit> tab) {
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars *bars = reinterpret_cast<Bars *>(smem + OFF_BAR);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    if ((smem_u32(smem) & 1023u) != 0) {  // SW128 tiles need 1024-byte alignment; uniform exit
-        if (threadIdx.x == 0) atomicOr(p.status, ST_PREFILL_SMEM_ALIGN);
+    // Split launches run in clusters: every thread takes part in both cluster barriers (the one after
+    // set-up and the one before exit), also on the uniform early exits below.
+    if constexpr (kSplit) {
+        if (threadIdx.x == 0) s_split_item = tab.cta_item[blockIdx.x];
+        __syncthreads();
+    }
+    const bool misaligned = (smem_u32(smem) & 1023u) != 0;  // SW128 tiles need 1024-byte alignment
+    if (misaligned || (kSplit && s_split_item < 0)) {
+        if (misaligned && threadIdx.x == 0) atomicOr(p.status, ST_PREFILL_SMEM_ALIGN);
+        if (kSplit) {
+            cluster_sync_all();
+            cluster_sync_all();
+        }
         return;
     }
     if (threadIdx.x == 0) {
@@ -840,6 +884,9 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         }
         mbar_init(&bars->drain, 2);  // one commit from each MMA issuer
         bars->abort = 0;
+        if (kSplit)
+            for (int x = 0; x < 2; ++x)
+                for (int q = 0; q < 4; ++q) mbar_init(&bars->recv[x][q], 1);
         fence_mbar_init();
         tma_prefetch_desc(&tm_qkv);
         tma_prefetch_desc(&tm_att);
@@ -859,13 +906,30 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         tmem_relinquish();
     }
     // Launched as a programmatic dependent: the set-up above touches no global memory, so it overlaps
-    // the previous kernel's tail; every global access (inputs, output, cache, workspace) follows this
+    // the previous kernel's tail; every global access (inputs, output, cache) follows this
     // wait. Dependents may start placing CTAs at once (they wait the same way before any access).
     grid_dependency_wait();
     grid_launch_dependents();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (kSplit) {
+        // A softmax warp whose 32 rows this CTA merges sets its receive barrier to expect the other
+        // chunks' bytes; their pushes follow the cluster barrier (the fence orders this before it).
+        if (warp >= SOFT_WARP0 && warp < EPI_WARP0 && lane == 0) {
+            const int x = (warp - SOFT_WARP0) / NSOFT_WARPS, q = warp & 3;
+            Item iu;
+            if (get_item<true>(p, 0, iu)) {
+                const int ncx = tile_chunks(p, iu.pair, x);
+                if (ncx > 1 && (4 * x + q) % ncx == iu.chunk) {
+                    mbar_arrive_expect_tx(&bars->recv[x][q], (ncx - 1) * PART_BYTES);
+                    fence_cluster();
+                }
+            }
+        }
+        __syncwarp();
+        cluster_arrive_relaxed();  // waited for by the softmax warps before their first push
+    }
     const uint32_t tbase = bars->tmem_base;
 
     if (warp < SOFT_WARP0) {  // WG0: the whole warpgroup gives registers back, then takes its roles
@@ -888,45 +952,110 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         run_epilogue<kSplit>(smem, bars, p, &tm_att, tbase, warp, lane);
     }
 
+    if (kSplit && (warp < SOFT_WARP0 || warp >= EPI_WARP0)) cluster_wait();  // (softmax warps waited)
     tc_fence_before();
     __syncthreads();
     if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tbase, TMEM_COLS);
     }
+    // No CTA of a cluster exits while a peer may still push into its shared memory.
+    if (kSplit) cluster_sync_all();
 }
 
 // ------------------------------------------------------------------ host side
 
-// Chunk size (K/V tiles per work unit) for a launch of n_pairs pairs per (head, sequence) on `sms`
-// SMs. Time model in units of one K/V tile step of a pair (both query tiles): a CTA's share of the
-// total work, or the longest single unit, whichever is larger. A unit costs its tiles plus a fixed
-// part measured on B200: ~2.2 steps for a whole pair (first loads, epilogue) and ~7 steps for a
-// split one (the partial rows' write-out, fences and the merge are a chain of memory round trips).
-// Large launches keep whole pairs; small ones (one layer of one sequence at P >= 1024) split the
-// long key ranges when that clearly shortens the longest unit.
-static int choose_kv_chunk(int n_qtiles, int n_pairs, long long hb, int sms) {
-    int best = n_qtiles;
-    double best_t = 1e300;
-    const int cs_min = std::max(2, (n_qtiles + MAX_CHUNKS - 1) / MAX_CHUNKS);
-    for (int cs = n_qtiles; cs >= cs_min; --cs) {
-        long long units = 0, tiles = 0;
-        for (int pr = 0; pr < n_pairs; ++pr) {
-            const int nkv = (2 * pr + 1 < n_qtiles) ? 2 * pr + 2 : 2 * pr + 1;
-            units += (nkv + cs - 1) / cs;
-            tiles += nkv;
-        }
-        const bool split = units > n_pairs;
-        const double ov = split ? 7.0 : 2.2;
-        const double share = (static_cast<double>(tiles) * hb + units * hb * ov) / sms;
-        const double longest = std::min(cs, n_qtiles) + ov;
-        const double t = std::max(share, longest);
-        if (t < best_t * 0.97) {  // prefer fewer, larger units unless splitting clearly pays
-            best_t = t;
-            best = cs;
+// Split launches. Time model in units of one K/V tile step of a pair (both query tiles): a unit costs
+// its K/V tiles plus a fixed part measured on B200 (first loads and the epilogue: ~2.2 steps for a
+// whole pair, SPLIT_OVERHEAD for a chunk, whose rows are also pushed to and merged in its cluster).
+// A split launch places every unit at once (one CTA each), so it costs its longest unit; it is used
+// when that clearly beats the longest whole pair.
+constexpr double WHOLE_OVERHEAD = 2.2;
+constexpr double SPLIT_OVERHEAD = 3.0;
+
+static int pair_kv_tiles_host(int n_qtiles, int pr) { return (2 * pr + 1 < n_qtiles) ? 2 * pr + 2 : 2 * pr + 1; }
+
+// Receive slots a CTA needs at most with chunk size cs: over every chunk k of every pair, the
+// partials of the other chunks for each 32-row group that k merges (group g of query tile x is merged
+// by chunk g % nx, nx = chunks holding x's keys).
+static int recv_slots_needed(int n_qtiles, int n_pairs, int cs) {
+    int need = 0;
+    for (int pr = 0; pr < n_pairs; ++pr) {
+        int nx[2];
+        for (int x = 0; x < 2; ++x) nx[x] = (2 * pr + x < n_qtiles) ? (2 * pr + x + cs) / cs : 0;
+        for (int k = 0; k < std::max(nx[0], nx[1]); ++k) {
+            int n = 0;
+            for (int g = 0; g < 8; ++g) {
+                const int c = nx[g >> 2];
+                if (c > 1 && g % c == k) n += c - 1;
+            }
+            need = std::max(need, n);
         }
     }
-    return best;
+    return need;
+}
+
+// Receive slots a split CTA has (recv_slot): the second Q buffer, the output slots and statistics, and
+// the K stages past the unit's at most cs K/V tiles.
+static int recv_slots_available(int cs) {
+    return RECV_Q_SLOTS + RECV_OUT_SLOTS + std::max(0, NSTAGE - cs) * TILE_BYTES / PART_BYTES;
+}
+
+// Places the units of a split launch, pairs in decreasing size, each pair's chunks on consecutive
+// ranks of one cluster of cl CTAs (first fit). Writes the CTA -> item table when `cta_item` is given
+// (entries of unused ranks stay as they are). Returns the number of clusters, or -1 above max_clusters.
+static int place_split_units(int n_qtiles, int n_pairs, int hb, int cs, int cl, int max_clusters,
+                             short *cta_item) {
+    int nc[64], ubase[64];
+    if (n_pairs > 64) return -1;
+    int u = 0;
+    for (int pr = n_pairs - 1; pr >= 0; --pr) {  // get_item's unit numbering: pairs from the last
+        nc[pr] = (pair_kv_tiles_host(n_qtiles, pr) + cs - 1) / cs;
+        ubase[pr] = u;
+        u += nc[pr];
+    }
+    int fill[MAX_SPLIT_CTAS];
+    int clusters = 0;
+    for (int pr = n_pairs - 1; pr >= 0; --pr) {
+        for (int b = 0; b < hb; ++b) {
+            int c = 0;
+            while (c < clusters && fill[c] + nc[pr] > cl) ++c;
+            if (c == clusters) {
+                if (clusters >= max_clusters || clusters >= MAX_SPLIT_CTAS) return -1;
+                fill[clusters++] = 0;
+            }
+            if (cta_item)
+                for (int k = 0; k < nc[pr]; ++k)
+                    cta_item[c * cl + fill[c] + k] = static_cast<short>((ubase[pr] + k) * hb + b);
+            fill[c] += nc[pr];
+        }
+    }
+    return clusters;
+}
+
+// Clusters of cl split CTAs that fit on the device at once (cached per context; 0 when unknown).
+static int max_active_clusters(DeviceContext *ctx, int cl) {
+    if (cl < 1 || cl > MAX_CLUSTER) return 0;
+    if (ctx->pf_active_clusters[cl] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(cl));
+        cfg.blockDim = dim3(NTHREADS);
+        cfg.dynamicSmemBytes = SMEM_BYTES;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_flash_prefill_tc<true>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = -1;
+        }
+        ctx->pf_active_clusters[cl] = n > 0 ? n : -1;
+    }
+    return std::max(0, ctx->pf_active_clusters[cl]);
 }
 
 }  // namespace prefill
@@ -963,33 +1092,6 @@ static void remember_map(int kind, const void *ptr, int E, int T, int B, long lo
     e = MapEntry{kind, device, E, T, B, ptr, seq_stride, true, map};
 }
 
-// Partial-row workspace of split prefill units (grown on demand, never while capturing).
-static bool ensure_prefill_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream) {
-    if (ctx->pf_part_floats >= floats && ctx->pf_counter_words >= words) return true;
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
-    if (cudaDeviceSynchronize() != cudaSuccess) return false;
-    // A grown buffer replaces the old one but the old one is never freed: a CUDA graph captured
-    // earlier keeps the address it was captured with. Growth at least doubles, so the retired
-    // buffers together stay below the live one.
-    if (ctx->pf_part_floats < floats) {
-        floats = std::max(floats, 2 * ctx->pf_part_floats);
-        ctx->pf_part = nullptr;
-        ctx->pf_part_floats = 0;
-        if (cudaMalloc(&ctx->pf_part, floats * sizeof(float)) != cudaSuccess) return false;
-        ctx->pf_part_floats = floats;
-    }
-    if (ctx->pf_counter_words < words) {
-        words = std::max(words, 2 * ctx->pf_counter_words);
-        ctx->pf_counters = nullptr;
-        ctx->pf_counter_words = 0;
-        if (cudaMalloc(&ctx->pf_counters, words * sizeof(unsigned)) != cudaSuccess) return false;
-        if (cudaMemset(ctx->pf_counters, 0, words * sizeof(unsigned)) != cudaSuccess) return false;
-        ctx->pf_counter_words = words;
-    }
-    return true;
-}
-
 // Launches the batched causal prefill. Arguments are validated by the caller (api.cu).
 int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
                    long long qkv_seq_stride, long long att_seq_stride, __half *kv_layer, int kv_maxT,
@@ -1000,7 +1102,8 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return GPT2_B200_EDEVICE;
     if (!ctx->prefill_attr_done) {
-        for (auto fn : {k_flash_prefill_tc<false>, k_flash_prefill_tc<true>}) {
+        for (const void *fn : {reinterpret_cast<const void *>(k_flash_prefill_tc<false>),
+                               reinterpret_cast<const void *>(k_flash_prefill_tc<true>)}) {
             // The warpgroups' register split is sized for exactly LAUNCH_REGS registers per thread at
             // launch; with any other count the softmax groups' setmaxnreg.inc could not be satisfied.
             cudaFuncAttributes fa;
@@ -1085,24 +1188,35 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
     p.kv_chunk = p.n_qtiles;  // whole pairs
     p.units_per_hb = p.n_pairs;
-    p.max_chunks = 1;
-    p.part = nullptr;
-    p.counters = nullptr;
+    // Fewer whole pairs than SMs: split the longest key ranges into chunks when one wave of clusters
+    // of the chunks clearly beats the longest whole pair.
+    int split_cs = 0, split_cl = 0, split_clusters = 0;
     if (hb * p.n_pairs < sms) {
-        const int cs = choose_kv_chunk(p.n_qtiles, p.n_pairs, hb, sms);
-        int units = 0;
-        for (int pr = 0; pr < p.n_pairs; ++pr)
-            units += (((2 * pr + 1 < p.n_qtiles) ? 2 * pr + 2 : 2 * pr + 1) + cs - 1) / cs;
-        const int max_chunks = (p.n_qtiles + cs - 1) / cs;
-        const size_t groups = static_cast<size_t>(hb) * p.n_pairs * 2;
-        if (units > p.n_pairs &&
-            ensure_prefill_workspace(ctx, groups * max_chunks * BM * PART_COLS, groups * 4, stream)) {
-            p.kv_chunk = cs;
-            p.units_per_hb = units;
-            p.max_chunks = max_chunks;
-            p.part = ctx->pf_part;
-            p.counters = ctx->pf_counters;
+        const int nkv_max = pair_kv_tiles_host(p.n_qtiles, p.n_pairs - 1);
+        double best = (nkv_max + WHOLE_OVERHEAD) * 0.97;
+        for (int cs = nkv_max - 1; cs >= 1; --cs) {
+            const int cl = (nkv_max + cs - 1) / cs;
+            if (cl > MAX_CLUSTER) break;
+            if (cs + SPLIT_OVERHEAD >= best) continue;
+            if (recv_slots_needed(p.n_qtiles, p.n_pairs, cs) > recv_slots_available(cs)) continue;
+            const int max_clusters = std::min(max_active_clusters(ctx, cl), std::min(sms, MAX_SPLIT_CTAS) / cl);
+            const int n = place_split_units(p.n_qtiles, p.n_pairs, static_cast<int>(hb), cs, cl, max_clusters, nullptr);
+            if (n <= 0) continue;
+            best = cs + SPLIT_OVERHEAD;
+            split_cs = cs;
+            split_cl = cl;
+            split_clusters = n;
         }
+    }
+    SplitTable tab;
+    if (split_cs > 0) {
+        for (int i = 0; i < MAX_SPLIT_CTAS; ++i) tab.cta_item[i] = -1;
+        place_split_units(p.n_qtiles, p.n_pairs, static_cast<int>(hb), split_cs, split_cl, split_clusters,
+                          tab.cta_item);
+        p.kv_chunk = split_cs;
+        p.units_per_hb = 0;
+        for (int pr = 0; pr < p.n_pairs; ++pr)
+            p.units_per_hb += (pair_kv_tiles_host(p.n_qtiles, pr) + split_cs - 1) / split_cs;
     }
     const long long total = static_cast<long long>(p.units_per_hb) * hb;
     if (total <= 0) return GPT2_B200_OK;
@@ -1111,21 +1225,27 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(HD)));
     p.status = ctx->status;
     p.timeout_ns = wait_timeout_ns();
-    // Persistent: at most CTAS_PER_SM resident CTAs per SM, each looping over its share of items.
-    const long long slots = static_cast<long long>(CTAS_PER_SM) * (ctx->num_sms > 0 ? ctx->num_sms : 148);
+    // Whole pairs: persistent, at most CTAS_PER_SM resident CTAs per SM, each looping over its share
+    // of items. Split: one CTA per unit in clusters of split_cl.
+    const long long slots = static_cast<long long>(CTAS_PER_SM) * sms;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(total < slots ? total : slots));
+    cfg.gridDim = dim3(static_cast<unsigned>(split_cs > 0 ? split_clusters * split_cl : (total < slots ? total : slots)));
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = SMEM_BYTES;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(split_cl);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t err = p.units_per_hb != p.n_pairs
-                                ? cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<true>, tm, tm_att, tm_kv, p)
-                                : cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<false>, tm, tm_att, tm_kv, p);
+    cfg.numAttrs = split_cs > 0 ? 2 : 1;
+    const cudaError_t err = split_cs > 0
+                                ? cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<true>, tm, tm_att, tm_kv, p, tab)
+                                : cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<false>, tm, tm_att, tm_kv, p,
+                                                     NoSplitTable{});
     return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 

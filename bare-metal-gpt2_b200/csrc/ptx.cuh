@@ -347,9 +347,14 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// The two halves of cluster_sync_all, for a barrier whose wait comes long after the arrival.
-__device__ __forceinline__ void cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+// The two halves of cluster_sync_all, for a barrier whose wait comes long after the arrival. The
+// arrival is relaxed: a thread whose earlier shared-memory writes peers must see after their wait
+// issues fence_cluster() first (mbarrier initialisation is published by fence_mbar_init).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_cluster() {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -364,15 +369,30 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_saddr, float4 v, ui
         "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cluster_bar)
         : "memory");
 }
+__device__ __forceinline__ void st_async_v2(uint32_t cluster_saddr, float a, float b, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                     cluster_saddr),
+                 "f"(a), "f"(b), "r"(cluster_bar)
+                 : "memory");
+}
 // Address of the same shared-memory location in the CTA of cluster rank `rank`.
 __device__ __forceinline__ uint32_t dsmem_addr(uint32_t local_saddr, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_saddr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_saddr) : "memory");
+// Loads from this CTA's shared memory by shared-window address.
+__device__ __forceinline__ float4 lds_v4(uint32_t saddr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(saddr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ float2 lds_v2(uint32_t saddr) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(saddr) : "memory");
     return v;
 }
 

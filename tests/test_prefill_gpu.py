@@ -176,10 +176,10 @@ def test_attention_with_kv_fill_rejects_bad_cache(cuda, lib):
 
 @pytest.mark.parametrize("T", [1400, 2048, 4096])
 def test_single_layer_long_prompts_split_path(cuda, lib, oracle, T):
-    """One layer of one long sequence: too few whole pairs to fill the SMs, so the key ranges of the
-    long query tiles are split across CTAs and merged (an odd tile count at T=1400 leaves a pair with
-    query tile A only; T=4096 reaches the cap of 8 chunks per pair). Checked against the oracle on a
-    sample of rows across the range, plus the last row."""
+    """One layer of one long sequence. At T=1400 and 2048 there are too few whole pairs to fill the SMs,
+    so the key ranges of the long query tiles are split into chunks run by the CTAs of a cluster and
+    merged there (an odd tile count at T=1400 leaves a pair with query tile A only); T=4096 has enough
+    whole pairs. Checked against the oracle on a sample of rows across the range, plus the last row."""
     torch = cuda
     x = O.seeded_qkv(4000 + T, T)
     att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
@@ -192,10 +192,26 @@ def test_single_layer_long_prompts_split_path(cuda, lib, oracle, T):
     assert_close(got[rows], ref[rows], f"T={T} sampled rows vs oracle")
 
 
+# (B, T) of split launches with clusters of 2, 3 and 4 chunks: T=640 / 1152 / 1536 for one sequence
+# (1152 fills every receive slot a CTA has: 6, the last in its unused K stage), B=2 at T=300 (one key
+# tile per chunk), 700 (ragged last tile) and 1024 (chunks of 4 tiles), B=3 at T=512.
+@pytest.mark.parametrize("B,T", [(1, 640), (1, 1152), (1, 1536), (2, 300), (2, 700), (2, 1024), (3, 512)])
+def test_split_units_cluster_shapes(cuda, lib, oracle, B, T):
+    torch = cuda
+    xs = [O.seeded_qkv(6100 + 7 * b + T, T) for b in range(B)]
+    att = torch.full((B, T, O.E), SENTINEL, dtype=torch.float16, device="cuda")
+    lib.prefill(att, dev16(torch, np.stack(xs)), T, B=B)
+    torch.cuda.synchronize()
+    assert lib.status() == 0
+    got = host(att)
+    for b in range(B):
+        assert_close(got[b], oracle.prefill(xs[b]), f"B={B} T={T} seq {b}")
+
+
 def test_single_layer_prefill_in_cuda_graph(cuda, lib, oracle):
-    """A one-layer launch takes the split-unit path, whose workspace is never allocated during stream
-    capture: captured before any eager call it keeps whole pairs, captured after one it replays the
-    split path. Both graphs must reproduce the eager result across replays."""
+    """A one-layer launch takes the split-unit path (clusters of chunks of a pair). Captured in a graph,
+    first before any eager call and then after one, it must reproduce the eager result across
+    replays."""
     torch = cuda
     T = 1024
     x = O.seeded_qkv(5150, T)
@@ -203,7 +219,7 @@ def test_single_layer_prefill_in_cuda_graph(cuda, lib, oracle):
     ref = oracle.prefill(x)
     s = torch.cuda.Stream()
     outs = []
-    for _ in range(2):  # first capture may predate the workspace; the eager call below creates it
+    for _ in range(2):  # the first capture precedes every eager split launch of this size
         att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
         g = torch.cuda.CUDAGraph()
         s.wait_stream(torch.cuda.current_stream())
