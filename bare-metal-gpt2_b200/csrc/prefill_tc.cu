@@ -94,6 +94,10 @@ constexpr int PART_BYTES = PART_O_BYTES + 32 * 8;
 constexpr int RECV_Q_SLOTS = 2 * TILE_BYTES / PART_BYTES;                   // 3
 constexpr int RECV_OUT_SLOTS = (OFF_BAR - OFF_OUT) / PART_BYTES;            // 2
 static_assert(RECV_Q_SLOTS == 3 && RECV_OUT_SLOTS == 2, "receive slots");
+// Split launches of single-query-tile units: (m, l) of the B group's rows, handed to the A group
+// (after the receive slots in the output-slot / statistics area).
+constexpr int OFF_XCH = OFF_BAR - BM * 8;
+static_assert(OFF_OUT + RECV_OUT_SLOTS * PART_BYTES <= OFF_XCH, "exchange area");
 constexpr int MAX_SPLIT_CTAS = 160;  // CTAs of a split launch at most (one unit each, <= the SM count)
 constexpr int NSOFT_WARPS = 4;  // per query tile: one warp per TMEM lane quarter
 // Four warpgroups, one warp of each on every SM sub-partition: WG0 = warps 0-3 (producer, the two MMA
@@ -142,6 +146,7 @@ struct __align__(8) Bars {
     uint64_t st_free[2][2];    // the epilogue has read them
     uint64_t drain;            // teardown: every MMA of both issuers has completed
     uint64_t recv[2][4];       // split launches: the pushed partial rows of [query tile][lane quarter]
+    uint64_t xm[4];            // single-query-tile split units: B's rows of a lane quarter are final
     uint32_t tmem_base;
     int abort;
 };
@@ -158,6 +163,7 @@ struct Params {
     int total_items;           // units_per_hb * H * B
     float scale_log2;          // log2(e) / sqrt(D)
     int kv_fill;               // also write K/V rows 0..T-1 into a KV-cache layer (B == 1)
+    int intra;                 // split launches: a unit is a chunk of ONE query tile's keys (see Item)
     unsigned *status;
     unsigned long long timeout_ns;
     __half *att;               // split launches: output rows are stored directly (no TMA slot)
@@ -174,12 +180,16 @@ struct NoSplitTable {};
 template <bool kSplit>
 using SplitArg = typename std::conditional<kSplit, SplitTable, NoSplitTable>::type;
 
+// A unit of work. Pair units: query tiles A = 2 pair and B = 2 pair + 1, both against K/V tiles
+// kv0 .. kv0 + nkv - 1 (A against a prefix). Single-query-tile units (split launches with
+// Params::intra): query tile `pair` against those tiles, its two softmax groups taking alternate
+// tiles (A the even ones, B the odd ones) and merging their rows at the end.
 struct Item {
     int pair, h, b;
-    int kv0;             // first K/V tile of this unit (its chunk of the pair's key range)
-    int chunk, nchunk;   // chunk index and chunks of this pair (nchunk > 1: partial rows + merge)
-    int nk[2];  // K/V tiles of query tile A (2p) and of B (2p+1, none past T) in this unit: a prefix
-    int nkv;    // K/V tiles loaded for the unit: max(nk)
+    int kv0;             // first K/V tile of this unit (its chunk of the key range)
+    int chunk, nchunk;   // chunk index and chunks of this key range (nchunk > 1: partial rows + merge)
+    int nk[2];  // K/V tiles group A and group B process in this unit
+    int nkv;    // K/V tiles loaded for the unit
     // nk[x] for a runtime x without a local-memory array access
     __device__ __forceinline__ int nk_of(int x) const { return x ? nk[1] : nk[0]; }
 };
@@ -236,6 +246,22 @@ __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
     const int rem = idx - u * per;
     it.b = static_cast<int>(div_magic(rem, p.H, p.h_magic, p.h_shift));
     it.h = rem - it.b * p.H;
+    if (kSplit && p.intra) {  // query tiles from the last, each in ceil((qt + 1) / kv_chunk) chunks
+        int qt = p.n_qtiles - 1, nc = (qt + p.kv_chunk) / p.kv_chunk;
+        while (qt > 0 && u >= nc) {
+            u -= nc;
+            --qt;
+            nc = (qt + p.kv_chunk) / p.kv_chunk;
+        }
+        it.pair = qt;
+        it.chunk = u;
+        it.nchunk = nc;
+        it.kv0 = u * p.kv_chunk;
+        it.nkv = min(it.kv0 + p.kv_chunk, qt + 1) - it.kv0;
+        it.nk[0] = (it.nkv + 1) >> 1;
+        it.nk[1] = it.nkv >> 1;
+        return true;
+    }
     int pr = p.n_pairs - 1 - u, nc = 1;  // whole pairs: unit u is pair n_pairs-1-u, one chunk
     if (kSplit) {
         for (pr = p.n_pairs - 1; pr > 0; --pr) {
@@ -256,6 +282,25 @@ __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
     it.nk[1] = (2 * pr + 1 < p.n_qtiles) ? hi - it.kv0 : 0;
     it.nkv = hi - it.kv0;
     return true;
+}
+
+// Whether query-tile group x processes K/V tile j of unit I, its first and last such tile (the last
+// only when it has any), and the query tile it works on.
+template <bool kSplit>
+__device__ __forceinline__ bool item_uses(const Params &p, const Item &I, int j, int x) {
+    return (kSplit && p.intra) ? ((j & 1) == x && j < I.nkv) : j < I.nk_of(x);
+}
+template <bool kSplit>
+__device__ __forceinline__ int item_first(const Params &p, int x) {
+    return (kSplit && p.intra) ? x : 0;
+}
+template <bool kSplit>
+__device__ __forceinline__ int item_last(const Params &p, const Item &I, int x) {
+    return (kSplit && p.intra) ? x + 2 * (I.nk_of(x) - 1) : I.nk_of(x) - 1;
+}
+template <bool kSplit>
+__device__ __forceinline__ int item_qtile(const Params &p, const Item &I, int x) {
+    return (kSplit && p.intra) ? I.pair : 2 * I.pair + x;
 }
 
 // A cursor over this CTA's K/V tiles in processing order (item by item).
@@ -310,7 +355,8 @@ __device__ void run_producer(const CUtensorMap *tm, const CUtensorMap *tm_kv, ui
     vc.start(p);
     auto owned = [&](const Cursor<kSplit> &c) -> int {
         const int tile = c.I.kv0 + c.j;
-        return (p.kv_fill && tile >= 2 * c.I.pair) ? (c.I.h << 16) | tile : -1;
+        const bool own = (kSplit && p.intra) ? tile == c.I.pair : tile >= 2 * c.I.pair;
+        return (p.kv_fill && own) ? (c.I.h << 16) | tile : -1;
     };
     // z = head for K, nHead + head for V (the layer's K block is followed by its V block)
     auto store_tile = [&](const uint8_t *src, int own, int zoff) {
@@ -338,11 +384,11 @@ __device__ void run_producer(const CUtensorMap *tm, const CUtensorMap *tm_kv, ui
         if (kc.j == 0) {  // new item: its two Q tiles (the buffer's previous item issued its last QK)
             const int qb = kc.it % NQ;
             if (kc.it >= NQ && !(ok = mbar_wait(&bars->q_empty[qb], ((kc.it / NQ) - 1) & 1, to))) break;
-            const int ntiles = kc.I.nk[1] ? 2 : 1;
+            const int ntiles = ((kSplit && p.intra) || !kc.I.nk[1]) ? 1 : 2;
             mbar_arrive_expect_tx(&bars->q_full[qb], ntiles * TILE_BYTES);
             for (int t = 0; t < ntiles; ++t)
                 tma_load_3d(smem + OFF_Q + (qb * 2 + t) * TILE_BYTES, tm, &bars->q_full[qb],
-                            kc.I.h * HD, (2 * kc.I.pair + t) * BM, kc.I.b);
+                            kc.I.h * HD, item_qtile<kSplit>(p, kc.I, t) * BM, kc.I.b);
             last_q[qb] = kc.it;
         }
         const int s = kc.g % NSTAGE;
@@ -429,13 +475,14 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
     // S = Q K^T for the K/V tile under cursor q (or release of that tile if this query tile skips it).
     auto qk_step = [&](const Cursor<kSplit> &q) -> bool {
         const int qb = q.it % NQ, s = q.g % NSTAGE;
-        const bool uses = q.j < q.I.nk_of(x);
+        const bool uses = item_uses<kSplit>(p, q.I, q.j, x);
         if (q.j == 0 && !warp_wait(&bars->q_full[qb], (q.it / NQ) & 1, to)) return false;
         if (!warp_wait(&bars->k_full[s], (q.g / NSTAGE) & 1, to)) return false;
         if (uses) {
             if (gs > 0 && !warp_wait(&S.s_free, (gs - 1) & 1, to)) return false;
             tc_fence_after();
-            const uint32_t a = ds.q_lo + (qb * 2 + x) * TILE_DESC, b = ds.k_lo + s * TILE_DESC;
+            const uint32_t a = ds.q_lo + (qb * 2 + ((kSplit && p.intra) ? 0 : x)) * TILE_DESC;
+            const uint32_t b = ds.k_lo + s * TILE_DESC;
             if (leader) {
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
@@ -448,7 +495,7 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
             mbar_arrive(&bars->k_empty[s]);
         }
         // the Q buffer: released after this query tile's last QK of the item (or at once if it has none)
-        const int last = q.I.nk_of(x) ? q.I.nk_of(x) - 1 : 0;
+        const int last = q.I.nk_of(x) ? item_last<kSplit>(p, q.I, x) : 0;
         if (q.j == last && leader) {
             if (uses) umma_commit(&bars->q_empty[qb]);
             else mbar_arrive(&bars->q_empty[qb]);
@@ -460,25 +507,26 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
     auto pv_step = [&](const Cursor<kSplit> &v) -> bool {
         const int s = v.g % NSTAGE;
         if (!warp_wait(&bars->v_full[s], (v.g / NSTAGE) & 1, to)) return false;
-        if (v.j >= v.I.nk_of(x)) {
+        if (!item_uses<kSplit>(p, v.I, v.j, x)) {
             if (leader) mbar_arrive(&bars->v_empty[s]);
             __syncwarp();
             return true;
         }
         if (!warp_wait(&S.p_full, gp & 1, to)) return false;
-        if (v.j == 0) {  // the item's first PV overwrites O: the epilogue must have read it
+        const bool first = v.j == item_first<kSplit>(p, x);
+        if (first) {  // the item's first PV overwrites O: the epilogue must have read it
             if (itp > 0 && !warp_wait(&S.o_free, (itp - 1) & 1, to)) return false;
             ++itp;
         }
         tc_fence_after();
         const uint32_t b = ds.v_lo + s * TILE_DESC;
         if (leader) {
-            umma_f16_ts_lohi(tO, tP, b, ds.v_hi, IDESC_O, v.j == 0 ? 0u : 1u);
+            umma_f16_ts_lohi(tO, tP, b, ds.v_hi, IDESC_O, first ? 0u : 1u);
 #pragma unroll
             for (int kk = 1; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P per step
                 umma_f16_ts_lohi(tO, tP + kk * 8, b + 128 * kk, ds.v_hi, IDESC_O, 1u);
             umma_commit(&S.o_done);
-            if (v.j == v.I.nk_of(x) - 1) umma_commit(&S.o_last);
+            if (v.j == item_last<kSplit>(p, v.I, x)) umma_commit(&S.o_last);
             umma_commit(&bars->v_empty[s]);
         }
         ++gp;
@@ -486,11 +534,12 @@ __device__ void run_mma(uint8_t *smem, Bars *bars, const Params &p, uint32_t tba
         return true;
     };
 
-    Cursor<kSplit> q, v;  // q: next K/V tile for QK; v: next tile for PV (one behind q)
+    Cursor<kSplit> q, v;  // q: next K/V tile for QK; v: next tile for PV (one behind q; two in
+                          // single-query-tile units, where this query tile uses every other K/V tile)
     q.start(p);
     v.start(p);
     bool ok = true;
-    if (q.valid) {
+    for (int lead = (kSplit && p.intra) ? 2 : 1; ok && lead > 0 && q.valid; --lead) {
         ok = qk_step(q);
         q.advance(p);
     }
@@ -622,6 +671,127 @@ __device__ __forceinline__ bool split_epilogue(uint8_t *smem, Bars *bars, const 
     return true;
 }
 
+// End of a single-query-tile unit of a split launch, run by each softmax warp for its 32 rows once its
+// group's last PV has completed. Group B hands its (m, l) to group A's warp of the same lane quarter
+// (its O stays in TMEM, which that warp can read); A combines both halves of the unit's key range.
+// With several chunks of the query tile, the merged rows of lane quarter q are then merged across the
+// cluster by chunk q % nchunk: the others push theirs into its shared memory (as the pair path does).
+// Returns false when a wait expired.
+__device__ __forceinline__ bool intra_epilogue(uint8_t *smem, Bars *bars, const Params &p, const Item &I,
+                                            uint32_t tl, int x, int quarter, int lane, int row, int g,
+                                            float m_row, float l_row) {
+    Stream &S = bars->st[x];
+    if (!warp_wait(&S.o_done, (g - 1) & 1, p.timeout_ns)) return false;  // this group's last PV
+    tc_fence_after();
+    float2 *xch = reinterpret_cast<float2 *>(smem + OFF_XCH);
+    if (x == 1) {
+        xch[row] = make_float2(m_row, l_row);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->xm[quarter]);
+        return true;
+    }
+    float o[HD];
+    {
+        uint32_t v[2][32];
+        tmem_ld32(tl + TCOL_O, v[0]);
+        tmem_ld32(tl + TCOL_O + 32, v[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] = __uint_as_float(v[i >> 5][i & 31]);
+    }
+    float m = m_row, l = l_row;
+    if (I.nk[1] > 0) {  // B's rows: wait for its hand-over, then combine
+        if (!warp_wait(&bars->xm[quarter], 0, p.timeout_ns)) return false;
+        tc_fence_after();
+        const float2 mlb = xch[row];
+        const float M = fmaxf(m, mlb.x);
+        const float wa = ex2_approx(m - M), wb = ex2_approx(mlb.x - M);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t v[32];
+            tmem_ld32(tl + TCOL_O + HD + 32 * h, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[32 * h + i] = fmaf(wb, __uint_as_float(v[i]), wa * o[32 * h + i]);
+        }
+        l = fmaf(wb, mlb.y, wa * l);
+        m = M;
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.o_free);
+    const int nc = I.nchunk;
+    const int km = nc > 1 ? quarter % nc : I.chunk;  // the chunk that merges these rows
+    int first = 0;  // the merging CTA's receive slots: after those of the quarters it merges before this one
+    for (int q2 = 0; q2 < quarter; ++q2)
+        if (q2 % nc == km) first += nc - 1;
+    if (I.chunk != km) {
+        const int slot = first + (I.chunk < km ? I.chunk : I.chunk - 1);
+        const uint32_t rank = cluster_rank() - static_cast<uint32_t>(I.chunk) + static_cast<uint32_t>(km);
+        const uint32_t dst = dsmem_addr(smem_u32(smem + recv_slot(slot, p.kv_chunk)), rank);
+        const uint32_t bar = dsmem_addr(smem_u32(&bars->recv[0][quarter]), rank);
+#pragma unroll
+        for (int c4 = 0; c4 < HD / 4; ++c4)
+            st_async_v4(dst + (c4 * 32 + lane) * 16, make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]),
+                        bar);
+        st_async_v2(dst + PART_O_BYTES + lane * 8, m, l, bar);
+        return true;
+    }
+    if (nc > 1) {
+        if (!warp_wait(&bars->recv[0][quarter], 0, p.timeout_ns)) return false;
+        const uint32_t in0 = smem_u32(smem) + static_cast<uint32_t>(lane) * 16u;
+        float mk[MAX_CLUSTER - 1], lk[MAX_CLUSTER - 1];
+        float M = m;
+#pragma unroll
+        for (int k = 0; k < MAX_CLUSTER - 1; ++k) {
+            mk[k] = -INFINITY;
+            lk[k] = 0.f;
+            if (k < nc - 1) {
+                const float2 ml = lds_v2(smem_u32(smem) + recv_slot(first + k, p.kv_chunk) + PART_O_BYTES + lane * 8);
+                mk[k] = ml.x;
+                lk[k] = ml.y;
+                M = fmaxf(M, ml.x);
+            }
+        }
+        const float ws = ex2_approx(m - M);
+        l *= ws;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] *= ws;
+#pragma unroll
+        for (int k = 0; k < MAX_CLUSTER - 1; ++k) {
+            if (k < nc - 1) {
+                const float w = ex2_approx(mk[k] - M);
+                l = fmaf(w, lk[k], l);
+                const uint32_t in = in0 + recv_slot(first + k, p.kv_chunk);
+                float4 q[HD / 4];
+#pragma unroll
+                for (int c4 = 0; c4 < HD / 4; ++c4) q[c4] = lds_v4(in + c4 * 512);
+#pragma unroll
+                for (int c4 = 0; c4 < HD / 4; ++c4) {
+                    o[4 * c4] = fmaf(w, q[c4].x, o[4 * c4]);
+                    o[4 * c4 + 1] = fmaf(w, q[c4].y, o[4 * c4 + 1]);
+                    o[4 * c4 + 2] = fmaf(w, q[c4].z, o[4 * c4 + 2]);
+                    o[4 * c4 + 3] = fmaf(w, q[c4].w, o[4 * c4 + 3]);
+                }
+            }
+        }
+    }
+    const float inv_l = 1.f / l;
+    const int qrow = I.pair * BM + row;
+    if (qrow < p.T) {
+        uint4 *dst = reinterpret_cast<uint4 *>(p.att + I.b * p.att_seq_stride + static_cast<long long>(qrow) * p.E +
+                                               I.h * HD);
+#pragma unroll
+        for (int q = 0; q < HD / 8; ++q)
+            dst[q] = make_uint4(pack_half2(o[8 * q] * inv_l, o[8 * q + 1] * inv_l),
+                                pack_half2(o[8 * q + 2] * inv_l, o[8 * q + 3] * inv_l),
+                                pack_half2(o[8 * q + 4] * inv_l, o[8 * q + 5] * inv_l),
+                                pack_half2(o[8 * q + 6] * inv_l, o[8 * q + 7] * inv_l));
+    }
+    return true;
+}
+
 // Softmax of query tile x (0 = A, 1 = B) of every item: 4 warps, thread = one query row (TMEM lane),
 // all 128 scores of a tile in registers. S is released as soon as it is in registers (the next QK
 // runs while this tile is processed). The packed P values are kept in registers until every
@@ -651,7 +821,12 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
     for (int it = 0; ok && get_item<kSplit>(p, it, I); ++it) {
         const int nk = I.nk_of(x);
         if (nk == 0) continue;     // this query tile has no keys in this unit of work
-        const int diag_j = 2 * I.pair + x - I.kv0;  // K/V tile holding this tile's diagonal
+        // this group's tile (in its own order) holding its query tile's diagonal, if any
+        int diag_j = 2 * I.pair + x - I.kv0;
+        if (kSplit && p.intra) {
+            const int jd = I.pair - I.kv0;
+            diag_j = (jd & 1) == x ? jd >> 1 : -1;
+        }
         float m_used = -INFINITY;  // running max (log2 units) used for the exponentials
         float l = 0.f;             // running sum of the (fp16-rounded) exponentials
         for (int j = 0; j < nk; ++j, ++g) {
@@ -738,7 +913,8 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
         }
         if (!ok) break;
         if (kSplit) {  // split launches: these warps finish their own rows (A and B in parallel)
-            ok = split_epilogue(smem, bars, p, I, tO, x, quarter, lane, row, g, m_used, l);
+            ok = p.intra ? intra_epilogue(smem, bars, p, I, tl, x, quarter, lane, row, g, m_used, l)
+                         : split_epilogue(smem, bars, p, I, tO, x, quarter, lane, row, g, m_used, l);
             if (!ok) break;
             continue;
         }
@@ -883,6 +1059,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
             }
         }
         mbar_init(&bars->drain, 2);  // one commit from each MMA issuer
+        if (kSplit)
+            for (int q = 0; q < 4; ++q) mbar_init(&bars->xm[q], 1);
         bars->abort = 0;
         if (kSplit)
             for (int x = 0; x < 2; ++x)
@@ -895,8 +1073,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         // drains (the producer's first loads, issued after the dependency wait, then hit L2).
         Item i0;
         if (get_item<kSplit>(p, 0, i0)) {
-            for (int t = 0; t < (i0.nk[1] ? 2 : 1); ++t)
-                tma_prefetch_l2_3d(&tm_qkv, i0.h * HD, (2 * i0.pair + t) * BM, i0.b);
+            for (int t = 0; t < (((kSplit && p.intra) || !i0.nk[1]) ? 1 : 2); ++t)
+                tma_prefetch_l2_3d(&tm_qkv, i0.h * HD, item_qtile<kSplit>(p, i0, t) * BM, i0.b);
             tma_prefetch_l2_3d(&tm_qkv, p.E + i0.h * HD, i0.kv0 * BN, i0.b);
             tma_prefetch_l2_3d(&tm_qkv, 2 * p.E + i0.h * HD, i0.kv0 * BN, i0.b);
         }
@@ -920,8 +1098,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
             const int x = (warp - SOFT_WARP0) / NSOFT_WARPS, q = warp & 3;
             Item iu;
             if (get_item<true>(p, 0, iu)) {
-                const int ncx = tile_chunks(p, iu.pair, x);
-                if (ncx > 1 && (4 * x + q) % ncx == iu.chunk) {
+                // pair units: group 4 x + q over the chunks holding x's keys; single-query-tile units:
+                // lane quarter q (merged by group A's warps) over all chunks
+                const int ncx = p.intra ? (x == 0 ? iu.nchunk : 0) : tile_chunks(p, iu.pair, x);
+                if (ncx > 1 && (p.intra ? q : 4 * x + q) % ncx == iu.chunk) {
                     mbar_arrive_expect_tx(&bars->recv[x][q], (ncx - 1) * PART_BYTES);
                     fence_cluster();
                 }
@@ -965,21 +1145,31 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
 
 // ------------------------------------------------------------------ host side
 
-// Split launches. Time model in units of one K/V tile step of a pair (both query tiles): a unit costs
-// its K/V tiles plus a fixed part measured on B200 (first loads and the epilogue: ~2.2 steps for a
-// whole pair, SPLIT_OVERHEAD for a chunk, whose rows are also pushed to and merged in its cluster).
-// A split launch places every unit at once (one CTA each), so it costs its longest unit; it is used
-// when that clearly beats the longest whole pair.
+// Split launches. Time model in units of one step of a unit (both softmax groups each process one K/V
+// tile, ~1.75 us): a unit costs its steps plus a fixed part fitted to back-to-back one-layer launches
+// on B200 (first loads, epilogue, and for split units the cluster barriers and merges): ~2.2 steps for
+// a whole pair, ~6 for a chunk of a pair, whose rows are pushed to and merged in its cluster, ~4.5 for
+// a chunk of one query tile, whose two groups merge locally and push a quarter of the rows per other
+// chunk. A split launch places every unit at once (one CTA each), so it costs its longest unit; it is
+// used when that clearly beats the longest whole pair.
 constexpr double WHOLE_OVERHEAD = 2.2;
-constexpr double SPLIT_OVERHEAD = 3.0;
+constexpr double SPLIT_OVERHEAD = 6.0;
+constexpr double INTRA_OVERHEAD = 4.5;
 
 static int pair_kv_tiles_host(int n_qtiles, int pr) { return (2 * pr + 1 < n_qtiles) ? 2 * pr + 2 : 2 * pr + 1; }
 
 // Receive slots a CTA needs at most with chunk size cs: over every chunk k of every pair, the
 // partials of the other chunks for each 32-row group that k merges (group g of query tile x is merged
-// by chunk g % nx, nx = chunks holding x's keys).
-static int recv_slots_needed(int n_qtiles, int n_pairs, int cs) {
+// by chunk g % nx, nx = chunks holding x's keys). Single-query-tile units: lane quarter q of a tile in
+// nc chunks is merged by chunk q % nc.
+static int recv_slots_needed(int n_qtiles, int n_pairs, int cs, bool intra) {
     int need = 0;
+    if (intra) {
+        const int nc = (n_qtiles - 1 + cs) / cs;  // the longest query tile's chunks
+        for (int n = 2; n <= nc; ++n)
+            for (int k = 0; k < n; ++k) need = std::max(need, ((3 - k) / n + 1) * (n - 1));
+        return need;
+    }
     for (int pr = 0; pr < n_pairs; ++pr) {
         int nx[2];
         for (int x = 0; x < 2; ++x) nx[x] = (2 * pr + x < n_qtiles) ? (2 * pr + x + cs) / cs : 0;
@@ -1001,22 +1191,31 @@ static int recv_slots_available(int cs) {
     return RECV_Q_SLOTS + RECV_OUT_SLOTS + std::max(0, NSTAGE - cs) * TILE_BYTES / PART_BYTES;
 }
 
-// Places the units of a split launch, pairs in decreasing size, each pair's chunks on consecutive
-// ranks of one cluster of cl CTAs (first fit). Writes the CTA -> item table when `cta_item` is given
-// (entries of unused ranks stay as they are). Returns the number of clusters, or -1 above max_clusters.
-static int place_split_units(int n_qtiles, int n_pairs, int hb, int cs, int cl, int max_clusters,
-                             short *cta_item) {
-    int nc[64], ubase[64];
-    if (n_pairs > 64) return -1;
+// Chunks of entry e of a (head, sequence) with chunk size cs: pair e, or query tile e of
+// single-query-tile units.
+static int entry_chunks(int n_qtiles, int e, int cs, bool intra) {
+    return intra ? (e + cs) / cs : (pair_kv_tiles_host(n_qtiles, e) + cs - 1) / cs;
+}
+
+// Places the units of a split launch, entries (pairs, or query tiles) in decreasing size, each entry's
+// chunks on consecutive ranks of one cluster of cl CTAs (first fit). Writes the CTA -> item table when
+// `cta_item` is given (entries of unused ranks stay as they are). Returns the number of clusters, or
+// -1 above max_clusters. Sets *units to the units per (head, sequence).
+static int place_split_units(int n_qtiles, int n_pairs, int hb, int cs, int cl, bool intra, int max_clusters,
+                             short *cta_item, int *units) {
+    const int n_entries = intra ? n_qtiles : n_pairs;
+    int nc[128], ubase[128];
+    if (n_entries > 128) return -1;
     int u = 0;
-    for (int pr = n_pairs - 1; pr >= 0; --pr) {  // get_item's unit numbering: pairs from the last
-        nc[pr] = (pair_kv_tiles_host(n_qtiles, pr) + cs - 1) / cs;
+    for (int pr = n_entries - 1; pr >= 0; --pr) {  // get_item's unit numbering: entries from the last
+        nc[pr] = entry_chunks(n_qtiles, pr, cs, intra);
         ubase[pr] = u;
         u += nc[pr];
     }
+    *units = u;
     int fill[MAX_SPLIT_CTAS];
     int clusters = 0;
-    for (int pr = n_pairs - 1; pr >= 0; --pr) {
+    for (int pr = n_entries - 1; pr >= 0; --pr) {
         for (int b = 0; b < hb; ++b) {
             int c = 0;
             while (c < clusters && fill[c] + nc[pr] > cl) ++c;
@@ -1071,6 +1270,34 @@ struct MapEntry {
 };
 constexpr int kMapCache = 8;
 thread_local MapEntry t_maps[kMapCache];
+
+// A launch's split plan (cs == 0: whole pairs) and its CTA -> unit table.
+struct SplitPlan {
+    int device, T, H, B;
+    int cs, cl, clusters, units;
+    bool intra;
+    b200::prefill::SplitTable tab;
+};
+constexpr int kPlanCache = 8;
+thread_local SplitPlan t_plans[kPlanCache];
+thread_local bool t_plan_valid[kPlanCache];
+thread_local int t_plan_next = 0;
+
+const SplitPlan *cached_split_plan(const DeviceContext *ctx, int T, int H, int B) {
+    for (int i = 0; i < kPlanCache; ++i)
+        if (t_plan_valid[i] && t_plans[i].device == ctx->device && t_plans[i].T == T && t_plans[i].H == H &&
+            t_plans[i].B == B)
+            return &t_plans[i];
+    return nullptr;
+}
+
+const SplitPlan *remember_split_plan(const SplitPlan &plan) {
+    const int i = t_plan_next;
+    t_plan_next = (t_plan_next + 1) % kPlanCache;
+    t_plans[i] = plan;
+    t_plan_valid[i] = true;
+    return &t_plans[i];
+}
 thread_local int t_map_next = 0;
 }  // namespace
 
@@ -1189,34 +1416,56 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     p.kv_chunk = p.n_qtiles;  // whole pairs
     p.units_per_hb = p.n_pairs;
     // Fewer whole pairs than SMs: split the longest key ranges into chunks when one wave of clusters
-    // of the chunks clearly beats the longest whole pair.
-    int split_cs = 0, split_cl = 0, split_clusters = 0;
-    if (hb * p.n_pairs < sms) {
-        const int nkv_max = pair_kv_tiles_host(p.n_qtiles, p.n_pairs - 1);
-        double best = (nkv_max + WHOLE_OVERHEAD) * 0.97;
-        for (int cs = nkv_max - 1; cs >= 1; --cs) {
-            const int cl = (nkv_max + cs - 1) / cs;
-            if (cl > MAX_CLUSTER) break;
-            if (cs + SPLIT_OVERHEAD >= best) continue;
-            if (recv_slots_needed(p.n_qtiles, p.n_pairs, cs) > recv_slots_available(cs)) continue;
-            const int max_clusters = std::min(max_active_clusters(ctx, cl), std::min(sms, MAX_SPLIT_CTAS) / cl);
-            const int n = place_split_units(p.n_qtiles, p.n_pairs, static_cast<int>(hb), cs, cl, max_clusters, nullptr);
-            if (n <= 0) continue;
-            best = cs + SPLIT_OVERHEAD;
-            split_cs = cs;
-            split_cl = cl;
-            split_clusters = n;
+    // of the chunks clearly beats the longest whole pair: chunks of pairs, or chunks of single query
+    // tiles whose two softmax groups take alternate K/V tiles (half the steps per chunk). The plan is
+    // host work that a back-to-back stream of one-layer launches would notice, so recent plans are
+    // kept per thread (the reference's forward pass calls attention with the same shape per layer).
+    const SplitPlan *plan = cached_split_plan(ctx, T, H, B);
+    if (!plan) {
+        SplitPlan np{};
+        np.device = ctx->device;
+        np.T = T;
+        np.H = H;
+        np.B = B;
+        if (hb * p.n_pairs < sms) {
+            const int nkv_max = pair_kv_tiles_host(p.n_qtiles, p.n_pairs - 1);
+            double best = (nkv_max + WHOLE_OVERHEAD) * 0.97;
+            for (int intra = 0; intra < 2; ++intra) {
+                const int longest = intra ? p.n_qtiles : nkv_max;  // K/V tiles of the longest entry
+                for (int cs = longest - (intra ? 0 : 1); cs >= 1; --cs) {
+                    const int cl = (longest + cs - 1) / cs;
+                    if (cl > MAX_CLUSTER) break;
+                    const double t = (intra ? (cs + 1) / 2 : cs) + (intra ? INTRA_OVERHEAD : SPLIT_OVERHEAD);
+                    if (t >= best) continue;
+                    if (recv_slots_needed(p.n_qtiles, p.n_pairs, cs, intra) > recv_slots_available(cs)) continue;
+                    const int max_clusters =
+                        std::min(max_active_clusters(ctx, cl), std::min(sms, MAX_SPLIT_CTAS) / cl);
+                    int units = 0;
+                    const int n = place_split_units(p.n_qtiles, p.n_pairs, static_cast<int>(hb), cs, cl,
+                                                    intra != 0, max_clusters, nullptr, &units);
+                    if (n <= 0) continue;
+                    best = t;
+                    np.cs = cs;
+                    np.cl = cl;
+                    np.clusters = n;
+                    np.units = units;
+                    np.intra = intra != 0;
+                }
+            }
         }
+        if (np.cs > 0) {
+            for (int i = 0; i < MAX_SPLIT_CTAS; ++i) np.tab.cta_item[i] = -1;
+            int units = 0;
+            place_split_units(p.n_qtiles, p.n_pairs, static_cast<int>(hb), np.cs, np.cl, np.intra, np.clusters,
+                              np.tab.cta_item, &units);
+        }
+        plan = remember_split_plan(np);
     }
-    SplitTable tab;
+    const int split_cs = plan->cs, split_cl = plan->cl, split_clusters = plan->clusters;
+    p.intra = plan->intra ? 1 : 0;
     if (split_cs > 0) {
-        for (int i = 0; i < MAX_SPLIT_CTAS; ++i) tab.cta_item[i] = -1;
-        place_split_units(p.n_qtiles, p.n_pairs, static_cast<int>(hb), split_cs, split_cl, split_clusters,
-                          tab.cta_item);
         p.kv_chunk = split_cs;
-        p.units_per_hb = 0;
-        for (int pr = 0; pr < p.n_pairs; ++pr)
-            p.units_per_hb += (pair_kv_tiles_host(p.n_qtiles, pr) + split_cs - 1) / split_cs;
+        p.units_per_hb = plan->units;
     }
     const long long total = static_cast<long long>(p.units_per_hb) * hb;
     if (total <= 0) return GPT2_B200_OK;
@@ -1243,7 +1492,7 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     cfg.attrs = attr;
     cfg.numAttrs = split_cs > 0 ? 2 : 1;
     const cudaError_t err = split_cs > 0
-                                ? cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<true>, tm, tm_att, tm_kv, p, tab)
+                                ? cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<true>, tm, tm_att, tm_kv, p, plan->tab)
                                 : cudaLaunchKernelEx(&cfg, k_flash_prefill_tc<false>, tm, tm_att, tm_kv, p,
                                                      NoSplitTable{});
     return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;

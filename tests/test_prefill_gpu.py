@@ -178,8 +178,9 @@ def test_attention_with_kv_fill_rejects_bad_cache(cuda, lib):
 def test_single_layer_long_prompts_split_path(cuda, lib, oracle, T):
     """One layer of one long sequence. At T=1400 and 2048 there are too few whole pairs to fill the SMs,
     so the key ranges of the long query tiles are split into chunks run by the CTAs of a cluster and
-    merged there (an odd tile count at T=1400 leaves a pair with query tile A only); T=4096 has enough
-    whole pairs. Checked against the oracle on a sample of rows across the range, plus the last row."""
+    merged there (T=1400: chunks of single query tiles, an odd tile count; T=2048: chunks of pairs);
+    T=4096 has enough whole pairs. Checked against the oracle on a sample of rows across the range,
+    plus the last row."""
     torch = cuda
     x = O.seeded_qkv(4000 + T, T)
     att = torch.empty((T, O.E), dtype=torch.float16, device="cuda")
@@ -192,10 +193,12 @@ def test_single_layer_long_prompts_split_path(cuda, lib, oracle, T):
     assert_close(got[rows], ref[rows], f"T={T} sampled rows vs oracle")
 
 
-# (B, T) of split launches with clusters of 2, 3 and 4 chunks: T=640 / 1152 / 1536 for one sequence
-# (1152 fills every receive slot a CTA has: 6, the last in its unused K stage), B=2 at T=300 (one key
-# tile per chunk), 700 (ragged last tile) and 1024 (chunks of 4 tiles), B=3 at T=512.
-@pytest.mark.parametrize("B,T", [(1, 640), (1, 1152), (1, 1536), (2, 300), (2, 700), (2, 1024), (3, 512)])
+# (B, T) of split launches. Single-query-tile units (the two softmax groups of a CTA take alternate
+# key tiles and merge locally): in clusters of 3 chunks (T=640), of 2 (T=1152, B=2 at T=512 and 640)
+# and unclustered (T=1536; B=2 at T=700, ragged last tile); chunks of pairs in clusters of 2 at
+# T=1792 (7-tile chunks, ragged). B=3 at T=512 keeps whole pairs.
+@pytest.mark.parametrize("B,T", [(1, 640), (1, 1152), (1, 1536), (1, 1792), (2, 512), (2, 640), (2, 700),
+                                 (3, 512)])
 def test_split_units_cluster_shapes(cuda, lib, oracle, B, T):
     torch = cuda
     xs = [O.seeded_qkv(6100 + 7 * b + T, T) for b in range(B)]
