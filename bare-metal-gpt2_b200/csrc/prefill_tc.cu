@@ -221,26 +221,17 @@ __device__ __forceinline__ int tile_chunks(const Params &p, int pair, int x) {
     return (2 * pair + x < p.n_qtiles) ? (2 * pair + x + p.kv_chunk) / p.kv_chunk : 0;
 }
 
-// Split launches: this CTA's unit (SplitTable::cta_item[blockIdx.x]), read once by thread 0 at launch.
-__shared__ int s_split_item;
+// Split launches: this CTA's unit (SplitTable::cta_item[blockIdx.x]), decoded once by thread 0 at
+// launch (before the grid dependency wait) for every role.
+__shared__ Item s_split_unit;
+__shared__ int s_split_valid;
 
-// The r-th work unit of this CTA. A unit is one chunk of kv_chunk K/V tiles of a pair of query tiles
-// (the whole key range unless the launch is too small to fill the SMs with whole pairs). Units are
-// numbered heaviest pair first; rounds alternate direction (snake) so that each CTA gets a mix of
-// heavy and light units. Returns false when this CTA has no r-th unit (nor any later one).
+// Work unit number idx: unit idx / (H B) of (head, sequence) idx % (H B). A unit is one chunk of
+// kv_chunk K/V tiles of a pair of query tiles (the whole key range unless the launch is too small to
+// fill the SMs with whole pairs), or of one query tile (Params::intra); units are numbered heaviest
+// pair (query tile) first.
 template <bool kSplit>
-__device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
-    int idx;
-    if (kSplit) {  // one unit per CTA, placed by the host
-        if (r > 0) return false;
-        idx = s_split_item;
-        if (idx < 0) return false;
-    } else {
-        const int G = gridDim.x, c = blockIdx.x;
-        const long long i = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - c) : c);
-        if (i >= p.total_items) return false;
-        idx = static_cast<int>(i);
-    }
+__device__ __forceinline__ void decode_item(const Params &p, int idx, Item &it) {
     const int per = p.H * p.B;
     int u = static_cast<int>(div_magic(idx, per, p.hb_magic, p.hb_shift));  // unit in its (head, seq)
     const int rem = idx - u * per;
@@ -260,7 +251,7 @@ __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
         it.nkv = min(it.kv0 + p.kv_chunk, qt + 1) - it.kv0;
         it.nk[0] = (it.nkv + 1) >> 1;
         it.nk[1] = it.nkv >> 1;
-        return true;
+        return;
     }
     int pr = p.n_pairs - 1 - u, nc = 1;  // whole pairs: unit u is pair n_pairs-1-u, one chunk
     if (kSplit) {
@@ -281,6 +272,22 @@ __device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
     it.nk[0] = max(0, min(hi, 2 * pr + 1) - it.kv0);
     it.nk[1] = (2 * pr + 1 < p.n_qtiles) ? hi - it.kv0 : 0;
     it.nkv = hi - it.kv0;
+}
+
+// The r-th work unit of this CTA. Whole-pair launches are persistent: rounds of one unit per CTA
+// alternate direction (snake) so that each CTA gets a mix of heavy and light units. Returns false
+// when this CTA has no r-th unit (nor any later one).
+template <bool kSplit>
+__device__ __forceinline__ bool get_item(const Params &p, int r, Item &it) {
+    if (kSplit) {  // one unit per CTA, placed by the host and decoded at launch
+        if (r > 0 || !s_split_valid) return false;
+        it = s_split_unit;
+        return true;
+    }
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long i = static_cast<long long>(r) * G + ((r & 1) ? (G - 1 - c) : c);
+    if (i >= p.total_items) return false;
+    decode_item<kSplit>(p, static_cast<int>(i), it);
     return true;
 }
 
@@ -1023,11 +1030,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     // Split launches run in clusters: every thread takes part in both cluster barriers (the one after
     // set-up and the one before exit), also on the uniform early exits below.
     if constexpr (kSplit) {
-        if (threadIdx.x == 0) s_split_item = tab.cta_item[blockIdx.x];
+        if (threadIdx.x == 0) {
+            const int idx = tab.cta_item[blockIdx.x];
+            s_split_valid = idx >= 0;
+            if (idx >= 0) decode_item<true>(p, idx, s_split_unit);
+        }
         __syncthreads();
     }
     const bool misaligned = (smem_u32(smem) & 1023u) != 0;  // SW128 tiles need 1024-byte alignment
-    if (misaligned || (kSplit && s_split_item < 0)) {
+    if (misaligned || (kSplit && !s_split_valid)) {
         if (misaligned && threadIdx.x == 0) atomicOr(p.status, ST_PREFILL_SMEM_ALIGN);
         if (kSplit) {
             cluster_sync_all();
