@@ -44,6 +44,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 EncodeTiledFn tensor_map_encoder() {
     // function-local static: initialised once, thread-safe
     static const EncodeTiledFn fn = [] {
+        RelaxedCapture relaxed;  // a first call may come while this thread captures a graph
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
@@ -74,9 +75,16 @@ DeviceContext *device_context() {
     DeviceContext &c = g_ctx[dev];
     c.num_sms = prop.multiProcessorCount;
     c.device = dev;
-    if (cudaMalloc(&c.status, sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(c.status, 0, sizeof(unsigned)) != cudaSuccess ||
-        cudaDeviceSynchronize() != cudaSuccess) {
+    // The first call of a process may be made while its thread captures a CUDA graph: the status word
+    // is allocated and zeroed on a private stream, which neither joins nor waits on a captured one.
+    RelaxedCapture relaxed;
+    cudaStream_t init = nullptr;
+    bool ok = cudaStreamCreateWithFlags(&init, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaMalloc(&c.status, sizeof(unsigned)) == cudaSuccess &&
+              cudaMemsetAsync(c.status, 0, sizeof(unsigned), init) == cudaSuccess &&
+              cudaStreamSynchronize(init) == cudaSuccess;
+    if (init) ok = cudaStreamDestroy(init) == cudaSuccess && ok;
+    if (!ok) {
         g_ctx_err[dev] = GPT2_B200_ECUDA;
         return nullptr;
     }

@@ -45,6 +45,17 @@ struct DeviceContext {
 // Returns the context of the current device (creating it on first use), or nullptr on CUDA error.
 DeviceContext *device_context();
 
+// Scope in which this thread's potentially unsafe CUDA calls (allocation, attribute set-up, occupancy
+// queries: one-time host work that enqueues nothing on the caller's stream) do not invalidate a
+// graph capture it may be running: the thread's capture mode is relaxed for the scope.
+struct RelaxedCapture {
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&mode); }
+    ~RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&mode); }
+    RelaxedCapture(const RelaxedCapture &) = delete;
+    RelaxedCapture &operator=(const RelaxedCapture &) = delete;
+};
+
 // The driver's cuTensorMapEncodeTiled, looked up once through the runtime (nullptr when the driver
 // lacks it). Shared by every kernel that builds TMA tensor maps.
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,

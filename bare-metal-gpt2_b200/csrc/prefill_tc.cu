@@ -1247,6 +1247,7 @@ static int place_split_units(int n_qtiles, int n_pairs, int hb, int cs, int cl, 
 static int max_active_clusters(DeviceContext *ctx, int cl) {
     if (cl < 1 || cl > MAX_CLUSTER) return 0;
     if (ctx->pf_active_clusters[cl] == 0) {
+        RelaxedCapture relaxed;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>(cl));
         cfg.blockDim = dim3(NTHREADS);
@@ -1340,6 +1341,7 @@ int launch_prefill(__half *att, const __half *qkv, int B, int T, int E, int H,
     EncodeTiledFn enc = tensor_map_encoder();
     if (!enc) return GPT2_B200_EDEVICE;
     if (!ctx->prefill_attr_done) {
+        RelaxedCapture relaxed;
         for (const void *fn : {reinterpret_cast<const void *>(k_flash_prefill_tc<false>),
                                reinterpret_cast<const void *>(k_flash_prefill_tc<true>)}) {
             // The warpgroups' register split is sized for exactly LAUNCH_REGS registers per thread at

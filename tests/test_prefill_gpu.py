@@ -243,3 +243,38 @@ def test_single_layer_prefill_in_cuda_graph(cuda, lib, oracle):
         outs.append(eager)
         del g
     assert lib.status() == 0
+
+
+def test_first_call_inside_graph_capture(cuda):
+    """A fresh process whose first prefill call (one layer, so the split path with its one-time
+    cluster occupancy query and kernel attribute set-up) is made while capturing a CUDA graph: the
+    capture must stay valid and the replay must match an eager call."""
+    import subprocess
+    import sys
+    code = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, %r)
+import gpt2_b200 as G
+lib = G.load()
+torch.cuda.set_device(0)
+T = 1024
+g = torch.Generator().manual_seed(7)
+qkv = torch.randn(T, 2304, generator=g).half().cuda()
+att = torch.empty(T, 768, dtype=torch.float16, device="cuda")
+s = torch.cuda.Stream()
+s.wait_stream(torch.cuda.current_stream())
+graph = torch.cuda.CUDAGraph()
+with torch.cuda.graph(graph, stream=s):
+    assert lib.gpt2_attention_b200_stream(att.data_ptr(), qkv.data_ptr(), T, 768, 12, 64, s.cuda_stream) == 0
+torch.cuda.current_stream().wait_stream(s)
+graph.replay()
+torch.cuda.synchronize()
+eager = torch.empty_like(att)
+lib.prefill(eager, qkv, T)
+torch.cuda.synchronize()
+assert lib.status() == 0
+assert torch.equal(att, eager), "replayed graph differs from the eager call"
+print("ok")
+""" % (os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bare-metal-gpt2_b200"),)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
