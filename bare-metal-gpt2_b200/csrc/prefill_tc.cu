@@ -38,14 +38,15 @@
 //                        swizzled 4 KB shared-memory slot per warp -> one TMA store of the warp's 32
 //                        rows, so output rows leave as whole 128-byte lines.
 //
-// Launches with fewer whole pairs than SMs (one layer of one sequence) run the kSplit instantiation:
-// a work unit is a chunk of a pair's key range, one unit per CTA, and the chunks of a pair run in one
-// thread-block cluster (up to 4 CTAs, placed by the host). At the end of its unit each softmax warp
-// of a chunk pushes its 32 unnormalised rows (o, m, l) into the shared memory of the CTA that merges
-// those rows (remote st.async stores that complete on an mbarrier there); the merging warp combines
-// them with its own rows and stores the output, so no partial row goes through global memory. With a
-// KV-cache target the producer also stores the K/V tiles its unit owns into the cache, straight from
-// the ring.
+// Launches with fewer whole pairs than SMs (one layer of one sequence) run the kSplit instantiation,
+// one work unit per CTA (placed by the host), the chunks of a key range in one thread-block cluster
+// (up to 4 CTAs). A unit is either a chunk of a pair's key range (both query tiles), or a chunk of ONE
+// query tile's key range whose K/V tiles the two softmax groups take in turn (A the even ones, B the
+// odd ones; they merge their rows locally at the end). Rows whose keys span several chunks are merged
+// by one chunk: the others push their unnormalised rows (o, m, l) into its shared memory (remote
+// st.async stores that complete on an mbarrier there), so no partial row goes through global memory.
+// With a KV-cache target the producer also stores the K/V tiles its unit owns into the cache,
+// straight from the ring.
 //
 // TMEM: all 512 columns (S_A at 0, S_B at 128, O_A 256, O_B 320, P_A 384, P_B 448). Shared memory:
 // Q 64 KB, K and V rings 128 KB, output slots 16 KB, row statistics 4 KB (split launches receive the
