@@ -879,17 +879,22 @@ __device__ void run_softmax(uint8_t *smem, Bars *bars, const Params &p, uint32_t
             }
             const float neg_m = -m_used;
             // P = 2^(s - m) as packed fp16 (kept in registers). The row sum adds the fp16-ROUNDED values
-            // (the ones the PV MMA consumes).
+            // (the ones the PV MMA consumes: numerator and denominator use identical weights). The
+            // scale-and-subtract runs two columns per instruction on the packed fp32 pipe; the block is
+            // bound by instruction issue, not by the MUFU.
             uint32_t pk[4][16];
             float ps[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) ps[k] = 0.f;
+            const uint64_t c2 = pair_f32(c, c), nm2 = pair_f32(neg_m, neg_m);
 #pragma unroll
             for (int cb = 0; cb < 4; ++cb) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float p0 = ex2_approx(fmaf(xs[32 * cb + 2 * i], c, neg_m));
-                    const float p1 = ex2_approx(fmaf(xs[32 * cb + 2 * i + 1], c, neg_m));
+                    float e0, e1;
+                    fma2_f32(e0, e1, xs[32 * cb + 2 * i], xs[32 * cb + 2 * i + 1], c2, nm2);
+                    const float p0 = ex2_approx(e0);
+                    const float p1 = ex2_approx(e1);
                     pk[cb][i] = pack_half2(p0, p1);
                     ps[(2 * i) & 7] = add_f16lo_f32(pk[cb][i], ps[(2 * i) & 7]);
                     ps[(2 * i + 1) & 7] = add_f16hi_f32(pk[cb][i], ps[(2 * i + 1) & 7]);

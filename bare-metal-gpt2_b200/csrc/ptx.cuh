@@ -457,6 +457,19 @@ __device__ __forceinline__ float add_f16hi_f32(uint32_t packed, float acc) {
     return r;
 }
 
+// Two fp32 lanes in one instruction (sm_100 packed fp32): (x, y) as one 64-bit register pair.
+__device__ __forceinline__ uint64_t pair_f32(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+// (ax * b.x + c.x, ay * b.y + c.y)
+__device__ __forceinline__ void fma2_f32(float &dx, float &dy, float ax, float ay, uint64_t b, uint64_t c) {
+    asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\tfma.rn.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(dx), "=f"(dy)
+        : "f"(ax), "f"(ay), "l"(b), "l"(c));
+}
+
 // max(a, b, c) in one instruction (sm_100 three-input max).
 __device__ __forceinline__ float max3f(float a, float b, float c) {
     float d;
