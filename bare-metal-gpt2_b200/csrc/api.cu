@@ -21,7 +21,7 @@ int launch_decode(__half *out, long long out_stride, const __half *q, long long 
                   const __half *kbase, const __half *vbase, long long kv_stride,
                   const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
                   int len_per_job, int len_add, int len, int max_len, int njobs, int H, int maxT,
-                  cudaStream_t stream, bool pdl = false);
+                  cudaStream_t stream, bool pdl = false, bool l2_early = false);
 int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream);
 size_t decode_workspace_floats(int jobs, int H, int max_len, int num_sms, size_t *words);
 int kv_alloc(GPT2KVCache *kv, int nLayer, int nHead, int headDim, int maxT);

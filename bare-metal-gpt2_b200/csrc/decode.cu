@@ -262,7 +262,7 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
                          const __half *kbase, const __half *vbase, long long kv_stride,
                          const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
                          int len_per_job, int len_add, int len, int max_len, int njobs, int H,
-                         int maxT, cudaStream_t stream, bool pdl);
+                         int maxT, cudaStream_t stream, bool pdl, bool l2_early = false);
 
 // Workspace the decode launches need for `jobs` (layer x sequence) decodes of up to max_len keys.
 size_t decode_workspace_floats(int jobs, int H, int max_len, int num_sms, size_t *words) {
@@ -278,10 +278,10 @@ int launch_decode(__half *out, long long out_stride, const __half *q, long long 
                   const __half *kbase, const __half *vbase, long long kv_stride,
                   const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
                   int len_per_job, int len_add, int len, int max_len, int njobs, int H, int maxT,
-                  cudaStream_t stream, bool pdl) {
+                  cudaStream_t stream, bool pdl, bool l2_early) {
     return launch_decode_stream(out, out_stride, q, q_stride, kbase, vbase, kv_stride, k_ptrs,
                                 v_ptrs, d_len, len_per_job, len_add, len, max_len, njobs, H, maxT,
-                                stream, pdl);
+                                stream, pdl, l2_early);
 }
 
 }  // namespace b200

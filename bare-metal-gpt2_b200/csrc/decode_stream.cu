@@ -19,6 +19,7 @@
 //     arrive merges them (atomic counter, re-armed to zero for the next call / graph replay).
 // Every mbarrier wait is bounded; a timeout sets a status bit and the CTA unwinds after its own
 // copies have landed.
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -48,6 +49,10 @@ struct __align__(8) Bars {
 //             Measured at 64 sequences x 12 heads: 3 stages 5.17 / 5.96 TB/s at 512 / 1023 keys,
 //             2 stages 5.02 / 5.73, 4 stages 4.89 / 5.56, 6 stages 3.99 / 4.58 (more CTAs per SM
 //             beat a deeper ring per CTA); 2 or 8 consumer warps are slower.
+//   NCW = 8:  64-key stages, 3-stage 48 KB ring, up to four CTAs per SM (between the two: about one
+//             to two SMs' worth of pairs, e.g. 8-24 sequences x 12 heads, where one CTA per pair
+//             per SM would leave SMs idle or run a second, partial wave; the pairs are split over
+//             the context so that one wave of CTAs loads every SM about equally).
 template <int NCW, int NSTAGE>
 struct Cfg {
     static constexpr int NT = 32 * (NCW + 1);
@@ -62,10 +67,13 @@ struct Cfg {
     static_assert(OFF_BAR % 8 == 0, "mbarriers need 8-byte alignment");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
-constexpr int NCW_FEW = 16, NCW_MANY = 4;
-constexpr int NSTAGE_FEW = 4, NSTAGE_MANY = 3;
+constexpr int NCW_FEW = 16, NCW_MANY = 4, NCW_MID = 8;
+constexpr int NSTAGE_FEW = 4, NSTAGE_MANY = 3, NSTAGE_MID = 3;
+constexpr int MID_PER_SM = 4;  // resident CTAs of the mid shape per SM (shared memory, registers)
 using CfgFew = Cfg<NCW_FEW, NSTAGE_FEW>;
 using CfgMany = Cfg<NCW_MANY, NSTAGE_MANY>;
+using CfgMid = Cfg<NCW_MID, NSTAGE_MID>;
+static_assert(MID_PER_SM * (CfgMid::SMEM_BYTES + 1024) <= 228 * 1024, "mid shape: four CTAs per SM");
 
 struct Params {
     const __half *q;
@@ -88,6 +96,9 @@ struct Params {
     unsigned *counters;       // [njobs][H]
     unsigned *status;
     unsigned long long timeout_ns;
+    // Inside a decode step only (0 elsewhere): bytes of K and of V per CTA that the producer requests
+    // into L2 before the grid dependency wait (see the kernel).
+    unsigned l2_early_bytes;
 };
 
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned long long to) {
@@ -96,7 +107,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsign
 }
 
 template <int NCW, int NSTAGE>
-__global__ void __launch_bounds__(32 * (NCW + 1)) k_decode_stream(const Params p) {
+__global__ void __launch_bounds__(32 * (NCW + 1), NCW == NCW_MID ? MID_PER_SM : NCW == NCW_MANY ? 8 : 1)
+    k_decode_stream(const Params p) {
     using C = Cfg<NCW, NSTAGE>;
     constexpr int KPS = C::KPS, STAGE_BYTES = C::STAGE_BYTES;
     constexpr int OFF_K = C::OFF_K, OFF_V = C::OFF_V, OFF_RED = C::OFF_RED, OFF_BAR = C::OFF_BAR;
@@ -109,7 +121,29 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) k_decode_stream(const Params p
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const unsigned long long to = p.timeout_ns;
     // Launched as a programmatic dependent (the batched decode step), the grid may start while its
-    // predecessor finishes; nothing it reads is touched before the predecessor has completed.
+    // predecessor finishes. Inside a decode step that predecessor is the QKV projection, which appends
+    // each sequence's newest K/V row; the lengths were written by a kernel that completed before the
+    // projection started, and every older row by an earlier step. So with l2_early_bytes set, the
+    // producer first requests this CTA's older rows into L2 (a prefetch reads nothing into the CTA
+    // and L2 is coherent), overlapping their HBM latency with the projection; everything the CTA
+    // reads follows the wait.
+    if (p.l2_early_bytes && t == NCW * 32) {
+        int len0 = p.len;
+        if (p.d_len) len0 = (p.len_per_job ? p.d_len[job] : p.d_len[0]) + p.len_add;
+        if (len0 >= 2 && len0 <= p.maxT) {
+            const int per0 = (len0 + p.nsplit - 1) / p.nsplit;
+            const int chunk0 = ((per0 + KPS - 1) / KPS) * KPS;
+            const int a = split * chunk0, b = min(a + chunk0, len0 - 1);  // rows before the newest
+            if (b > a) {
+                const uint32_t bytes = min(static_cast<uint32_t>(b - a) * ROW_BYTES, p.l2_early_bytes);
+                const __half *K0 = p.k_ptrs ? p.k_ptrs[job] : p.kbase + job * p.kv_stride;
+                const __half *V0 = p.v_ptrs ? p.v_ptrs[job] : p.vbase + job * p.kv_stride;
+                const long long off = static_cast<long long>(h) * p.maxT * HD + static_cast<long long>(a) * HD;
+                bulk_prefetch_l2(K0 + off, bytes);
+                bulk_prefetch_l2(V0 + off, bytes);
+            }
+        }
+    }
     grid_dependency_wait();
     grid_launch_dependents();
 
@@ -342,17 +376,42 @@ __global__ void __launch_bounds__(32 * (NCW + 1)) k_decode_stream(const Params p
 
 }  // namespace dstream
 
+struct DecodeStreamPlan {
+    int shape;   // 0: one CTA per SM (16 consumer warps), 1: mid (8 warps), 2: many small CTAs (4 warps)
+    int nsplit;  // CTAs per (job, head)
+};
+
 int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream);
 
-// CTAs per (job, head): about one CTA per SM in total, at least one stage per CTA.
-int decode_stream_splits(int max_len, long long pairs, int num_sms) {
+// Shape and split of a launch over `pairs` (job, head) pairs of up to max_len keys, in one wave of
+// CTAs. A split pair costs a merge of partial rows through global memory by the last CTA to finish
+// (a chain of L2 round trips at the end of the launch), so pairs are split only when whole pairs
+// would leave more than half of the SMs idle:
+//   pairs <= SMs / 2       one CTA per SM, each pair split over floor(SMs / pairs) CTAs;
+//   SMs / 2 < pairs <= SMs one CTA per SM, pairs whole;
+//   SMs < pairs < 2 SMs    the mid shape (up to four CTAs per SM), pairs whole: one wave, instead
+//                          of a second, partial wave of one-per-SM CTAs;
+//   pairs >= 2 SMs         the small shape, pairs whole.
+// Measured, 12-layer decode step at context 500-1023: 8 sequences (96 pairs) 69.6 us of attention
+// with whole pairs against 135 us split in two (192 one-per-SM CTAs: a partial second wave) and
+// 100 us split in three in the mid shape.
+DecodeStreamPlan decode_stream_plan(int max_len, long long pairs, int num_sms) {
     const int sms = num_sms > 0 ? num_sms : 148;
-    long long n = (sms + pairs / 2) / pairs;  // round(sms / pairs)
-    if (n < 1) n = 1;
-    const long long max_n = (max_len + dstream::CfgFew::KPS - 1) /
-                            dstream::CfgFew::KPS;
-    if (n > max_n) n = max_n;
-    return static_cast<int>(n);
+    DecodeStreamPlan plan{0, 1};
+    if (pairs >= 2LL * sms) {
+        plan.shape = 2;
+    } else if (pairs > sms) {
+        plan.shape = 1;
+    } else if (2 * pairs <= sms) {
+        const long long max_n = std::max(1, (max_len + dstream::CfgFew::KPS - 1) / dstream::CfgFew::KPS);
+        plan.nsplit = static_cast<int>(std::max(1LL, std::min(max_n, sms / pairs)));
+    }
+    return plan;
+}
+
+// CTAs per (job, head) of a launch (sizes the split workspace).
+int decode_stream_splits(int max_len, long long pairs, int num_sms) {
+    return decode_stream_plan(max_len, pairs, num_sms).nsplit;
 }
 
 // Sets the kernel's shared-memory attribute on the current device (once), so that a later launch
@@ -366,7 +425,10 @@ int prepare_decode_stream() {
                                  dstream::CfgFew::SMEM_BYTES) != cudaSuccess ||
             cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 dstream::CfgMany::SMEM_BYTES) != cudaSuccess)
+                                 dstream::CfgMany::SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(dstream::k_decode_stream<dstream::NCW_MID, dstream::NSTAGE_MID>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 dstream::CfgMid::SMEM_BYTES) != cudaSuccess)
             return GPT2_B200_ECUDA;
         ctx->decode_attr_done = true;
     }
@@ -377,7 +439,7 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
                          const __half *kbase, const __half *vbase, long long kv_stride,
                          const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
                          int len_per_job, int len_add, int len, int max_len, int njobs, int H,
-                         int maxT, cudaStream_t stream, bool pdl) {
+                         int maxT, cudaStream_t stream, bool pdl, bool l2_early) {
     DeviceContext *ctx = device_context();
     if (!ctx) return GPT2_B200_ECUDA;
     if (!ctx->decode_attr_done && prepare_decode_stream() != GPT2_B200_OK) return GPT2_B200_ECUDA;
@@ -398,7 +460,8 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
     p.H = H;
     p.maxT = maxT;
     p.njobs = njobs;
-    p.nsplit = decode_stream_splits(max_len, static_cast<long long>(njobs) * H, ctx->num_sms);
+    const DecodeStreamPlan plan = decode_stream_plan(max_len, static_cast<long long>(njobs) * H, ctx->num_sms);
+    p.nsplit = plan.nsplit;
     p.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
     p.status = ctx->status;
     p.timeout_ns = wait_timeout_ns();
@@ -412,12 +475,16 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
         p.part = ctx->part;
         p.counters = ctx->counters;
     }
+    // At most ~40 MB requested into L2 per launch (of the 126 MB), 256 KB of K and of V per CTA.
+    const long long ctas = static_cast<long long>(p.nsplit) * H * njobs;
+    const long long cap = std::min(256LL << 10, (40LL << 20) / (2 * ctas)) & ~15LL;
+    p.l2_early_bytes = (l2_early && pdl && d_len) ? static_cast<unsigned>(cap) : 0u;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.nsplit, H, njobs);
-    // Many (job, head) pairs, each whole in one CTA: the small CTA shape, several per SM.
-    const bool many = p.nsplit == 1 && static_cast<long long>(njobs) * H >= 2LL * ctx->num_sms;
-    cfg.blockDim = dim3(many ? dstream::CfgMany::NT : dstream::CfgFew::NT, 1, 1);
-    cfg.dynamicSmemBytes = many ? dstream::CfgMany::SMEM_BYTES : dstream::CfgFew::SMEM_BYTES;
+    cfg.blockDim = dim3(plan.shape == 2 ? dstream::CfgMany::NT
+                        : plan.shape == 1 ? dstream::CfgMid::NT : dstream::CfgFew::NT, 1, 1);
+    cfg.dynamicSmemBytes = plan.shape == 2 ? dstream::CfgMany::SMEM_BYTES
+                           : plan.shape == 1 ? dstream::CfgMid::SMEM_BYTES : dstream::CfgFew::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -425,8 +492,9 @@ int launch_decode_stream(__half *out, long long out_stride, const __half *q, lon
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     const cudaError_t err =
-        many ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>, p)
-             : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW, dstream::NSTAGE_FEW>, p);
+        plan.shape == 2 ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MANY, dstream::NSTAGE_MANY>, p)
+        : plan.shape == 1 ? cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_MID, dstream::NSTAGE_MID>, p)
+                          : cudaLaunchKernelEx(&cfg, dstream::k_decode_stream<dstream::NCW_FEW, dstream::NSTAGE_FEW>, p);
     return err == cudaSuccess ? GPT2_B200_OK : GPT2_B200_ECUDA;
 }
 

@@ -36,7 +36,7 @@ int launch_decode(__half *out, long long out_stride, const __half *q, long long 
                   const __half *kbase, const __half *vbase, long long kv_stride,
                   const __half *const *k_ptrs, const __half *const *v_ptrs, const int *d_len,
                   int len_per_job, int len_add, int len, int max_len, int njobs, int H, int maxT,
-                  cudaStream_t stream, bool pdl = false);
+                  cudaStream_t stream, bool pdl = false, bool l2_early = false);
 int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cudaStream_t stream);
 size_t decode_workspace_floats(int jobs, int H, int max_len, int num_sms, size_t *words);
 int prepare_decode_stream();
@@ -255,12 +255,13 @@ int enqueue_step(gpt2_b200_batch *bt, const int *d_tok, const int *d_pos, __half
         }
         // The attention joins the launch chain only with few (sequence, head) pairs (one CTA per
         // pair per SM); with many pairs its small-CTA shape runs faster as an ordinary launch
-        // (64 sequences: step 651 vs 663 us; 8 sequences chained: 422.5 vs 428 us).
+        // (64 sequences: step 651 vs 663 us; 8 sequences chained: 422.5 vs 428 us). Chained, it
+        // requests each sequence's older K/V rows into L2 while this layer's QKV projection runs.
         const bool attn_pdl = bt->pdl && static_cast<long long>(B) * NH < 2LL * ctx->num_sms;
         rc = launch_decode(bt->att, E, bt->qkv, Q, nullptr, nullptr, 0,
                            bt->kslab + static_cast<size_t>(L) * B,
                            bt->vslab + static_cast<size_t>(L) * B, d_pos, 1, 1, 0, bt->maxT, B, NH,
-                           bt->maxT, st, attn_pdl);
+                           bt->maxT, st, attn_pdl, attn_pdl);
         if (rc != GPT2_B200_OK) return rc;
         if (attention_only) continue;
         if ((rc = lin::launch_linear(bt->proj_p[L], st)) != GPT2_B200_OK) return rc;

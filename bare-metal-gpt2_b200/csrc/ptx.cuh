@@ -140,6 +140,13 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// Prefetch of `bytes` contiguous bytes into L2 (16-byte aligned address and size; no shared memory, no
+// completion to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+                 "r"(bytes)
+                 : "memory");
+}
 // Prefetch of one 3-D box into L2 (no shared memory, no completion to wait for). It only warms L2,
 // which is coherent for the whole GPU, so it may run before a grid dependency wait: a later load still
 // returns what the producing kernel wrote.

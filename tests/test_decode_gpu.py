@@ -140,14 +140,15 @@ def test_decode_batched_sequences(cuda, lib, oracle, cache):
         assert_close(got[b], want, f"seq {b} (layer {L}, len {n})")
 
 
-def test_decode_batched_many_sequences(cuda, lib, oracle, cache):
-    """Enough (sequence, head) pairs for the small-CTA shape (several CTAs per SM, each pair whole in
-    one CTA): 40 sequences x 12 heads, lengths covering stage edges of 32 keys and the full cache."""
+@pytest.mark.parametrize("B", [40, 8, 13, 16, 24])
+def test_decode_batched_many_sequences(cuda, lib, oracle, cache, B):
+    """Batches of sequences: 40 x 12 heads takes the small-CTA shape (several CTAs per SM, each pair
+    whole in one CTA); 8, 13, 16 and 24 sequences (96-288 pairs) the mid shape, each pair split over
+    the context. Lengths cover the stage edges of 32 and 64 keys and the full cache."""
     torch = cuda
-    rng = np.random.default_rng(77)
-    lens = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1023, 1024] + \
-        [int(x) for x in rng.integers(1, MAXT + 1, size=27)]
-    B = len(lens)
+    rng = np.random.default_rng(77 + B)
+    edges = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1023, 1024]
+    lens = (edges + [int(x) for x in rng.integers(1, MAXT + 1, size=max(0, B - len(edges)))])[:B]
     slab = O.H * MAXT * O.D
     base = cache["d_arena"].data_ptr()
     layers = [b % L_ for b in range(B)]
