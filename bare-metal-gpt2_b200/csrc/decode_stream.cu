@@ -49,10 +49,9 @@ struct __align__(8) Bars {
 //             Measured at 64 sequences x 12 heads: 3 stages 5.17 / 5.96 TB/s at 512 / 1023 keys,
 //             2 stages 5.02 / 5.73, 4 stages 4.89 / 5.56, 6 stages 3.99 / 4.58 (more CTAs per SM
 //             beat a deeper ring per CTA); 2 or 8 consumer warps are slower.
-//   NCW = 8:  64-key stages, 3-stage 48 KB ring, up to four CTAs per SM (between the two: about one
-//             to two SMs' worth of pairs, e.g. 8-24 sequences x 12 heads, where one CTA per pair
-//             per SM would leave SMs idle or run a second, partial wave; the pairs are split over
-//             the context so that one wave of CTAs loads every SM about equally).
+//   NCW = 8:  64-key stages, 3-stage 48 KB ring, up to four CTAs per SM (between the two: one to
+//             four SMs' worth of pairs, e.g. 13-49 sequences x 12 heads, where one CTA per pair
+//             per SM would run a second, partial wave; each pair whole in one CTA, all in one wave).
 template <int NCW, int NSTAGE>
 struct Cfg {
     static constexpr int NT = 32 * (NCW + 1);
@@ -389,16 +388,17 @@ int ensure_decode_workspace(DeviceContext *ctx, size_t floats, size_t words, cud
 // would leave more than half of the SMs idle:
 //   pairs <= SMs / 2       one CTA per SM, each pair split over floor(SMs / pairs) CTAs;
 //   SMs / 2 < pairs <= SMs one CTA per SM, pairs whole;
-//   SMs < pairs < 2 SMs    the mid shape (up to four CTAs per SM), pairs whole: one wave, instead
+//   SMs < pairs <= 4 SMs   the mid shape (up to four CTAs per SM), pairs whole: one wave, instead
 //                          of a second, partial wave of one-per-SM CTAs;
-//   pairs >= 2 SMs         the small shape, pairs whole.
+//   pairs > 4 SMs          the small shape (eight CTAs per SM), pairs whole.
 // Measured, 12-layer decode step at context 500-1023: 8 sequences (96 pairs) 69.6 us of attention
 // with whole pairs against 135 us split in two (192 one-per-SM CTAs: a partial second wave) and
-// 100 us split in three in the mid shape.
+// 100 us split in three in the mid shape; 16 sequences 110.6 us in the mid shape against 127 us in
+// two waves; 32 sequences (384 pairs) 140.6 us in the mid shape against 150.9 us in the small one.
 DecodeStreamPlan decode_stream_plan(int max_len, long long pairs, int num_sms) {
     const int sms = num_sms > 0 ? num_sms : 148;
     DecodeStreamPlan plan{0, 1};
-    if (pairs >= 2LL * sms) {
+    if (pairs > 4LL * sms) {
         plan.shape = 2;
     } else if (pairs > sms) {
         plan.shape = 1;

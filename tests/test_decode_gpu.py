@@ -140,11 +140,12 @@ def test_decode_batched_sequences(cuda, lib, oracle, cache):
         assert_close(got[b], want, f"seq {b} (layer {L}, len {n})")
 
 
-@pytest.mark.parametrize("B", [40, 8, 13, 16, 24])
+@pytest.mark.parametrize("B", [64, 8, 13, 16, 24, 40])
 def test_decode_batched_many_sequences(cuda, lib, oracle, cache, B):
-    """Batches of sequences: 40 x 12 heads takes the small-CTA shape (several CTAs per SM, each pair
-    whole in one CTA); 8, 13, 16 and 24 sequences (96-288 pairs) the mid shape, each pair split over
-    the context. Lengths cover the stage edges of 32 and 64 keys and the full cache."""
+    """Batches of sequences, each (sequence, head) pair whole in one CTA: 64 x 12 heads takes the
+    small-CTA shape (eight CTAs per SM), 13-40 sequences (156-480 pairs) the mid shape (up to four per
+    SM), 8 sequences one CTA per SM. Lengths cover the stage edges of 32, 64 and 128 keys and the
+    full cache."""
     torch = cuda
     rng = np.random.default_rng(77 + B)
     edges = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1023, 1024]
