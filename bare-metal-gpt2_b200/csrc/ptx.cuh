@@ -235,6 +235,44 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+// 32 lanes x 64 consecutive 32-bit columns in one instruction: thread t receives row (lane base + t),
+// columns [taddr.col, taddr.col + 64) as r[c / 32][c % 32].
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[2][32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32"
+        " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+        : "=r"(r[0][0]), "=r"(r[0][1]), "=r"(r[0][2]), "=r"(r[0][3]), "=r"(r[0][4]), "=r"(r[0][5]),
+          "=r"(r[0][6]), "=r"(r[0][7]), "=r"(r[0][8]), "=r"(r[0][9]), "=r"(r[0][10]), "=r"(r[0][11]),
+          "=r"(r[0][12]), "=r"(r[0][13]), "=r"(r[0][14]), "=r"(r[0][15]), "=r"(r[0][16]), "=r"(r[0][17]),
+          "=r"(r[0][18]), "=r"(r[0][19]), "=r"(r[0][20]), "=r"(r[0][21]), "=r"(r[0][22]), "=r"(r[0][23]),
+          "=r"(r[0][24]), "=r"(r[0][25]), "=r"(r[0][26]), "=r"(r[0][27]), "=r"(r[0][28]), "=r"(r[0][29]),
+          "=r"(r[0][30]), "=r"(r[0][31]), "=r"(r[1][0]), "=r"(r[1][1]), "=r"(r[1][2]), "=r"(r[1][3]),
+          "=r"(r[1][4]), "=r"(r[1][5]), "=r"(r[1][6]), "=r"(r[1][7]), "=r"(r[1][8]), "=r"(r[1][9]),
+          "=r"(r[1][10]), "=r"(r[1][11]), "=r"(r[1][12]), "=r"(r[1][13]), "=r"(r[1][14]), "=r"(r[1][15]),
+          "=r"(r[1][16]), "=r"(r[1][17]), "=r"(r[1][18]), "=r"(r[1][19]), "=r"(r[1][20]), "=r"(r[1][21]),
+          "=r"(r[1][22]), "=r"(r[1][23]), "=r"(r[1][24]), "=r"(r[1][25]), "=r"(r[1][26]), "=r"(r[1][27]),
+          "=r"(r[1][28]), "=r"(r[1][29]), "=r"(r[1][30]), "=r"(r[1][31])
+        : "r"(taddr));
+}
+// 32 lanes x 64 consecutive 32-bit columns in one instruction (r[c / 16][c % 16] -> column c).
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[4][16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x64.b32"
+        " [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};"
+        :: "r"(taddr),
+        "r"(r[0][0]), "r"(r[0][1]), "r"(r[0][2]), "r"(r[0][3]), "r"(r[0][4]), "r"(r[0][5]),
+        "r"(r[0][6]), "r"(r[0][7]), "r"(r[0][8]), "r"(r[0][9]), "r"(r[0][10]), "r"(r[0][11]),
+        "r"(r[0][12]), "r"(r[0][13]), "r"(r[0][14]), "r"(r[0][15]), "r"(r[1][0]), "r"(r[1][1]),
+        "r"(r[1][2]), "r"(r[1][3]), "r"(r[1][4]), "r"(r[1][5]), "r"(r[1][6]), "r"(r[1][7]),
+        "r"(r[1][8]), "r"(r[1][9]), "r"(r[1][10]), "r"(r[1][11]), "r"(r[1][12]), "r"(r[1][13]),
+        "r"(r[1][14]), "r"(r[1][15]), "r"(r[2][0]), "r"(r[2][1]), "r"(r[2][2]), "r"(r[2][3]),
+        "r"(r[2][4]), "r"(r[2][5]), "r"(r[2][6]), "r"(r[2][7]), "r"(r[2][8]), "r"(r[2][9]),
+        "r"(r[2][10]), "r"(r[2][11]), "r"(r[2][12]), "r"(r[2][13]), "r"(r[2][14]), "r"(r[2][15]),
+        "r"(r[3][0]), "r"(r[3][1]), "r"(r[3][2]), "r"(r[3][3]), "r"(r[3][4]), "r"(r[3][5]),
+        "r"(r[3][6]), "r"(r[3][7]), "r"(r[3][8]), "r"(r[3][9]), "r"(r[3][10]), "r"(r[3][11]),
+        "r"(r[3][12]), "r"(r[3][13]), "r"(r[3][14]), "r"(r[3][15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32"
