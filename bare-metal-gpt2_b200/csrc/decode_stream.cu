@@ -6,8 +6,10 @@
 //
 // Decode is a pure HBM stream (36,864 bytes of K+V per key for the 12-layer step), so the kernel is
 // built to keep every SM's share of HBM busy from start to finish:
-//   - grid = (split, head, job) sized to about one CTA per SM; for the 12-layer GPT-2 step that is
-//     one CTA per (layer, head) streaming its whole context, so no cross-CTA merge is needed at all;
+//   - grid = (split, head, job), always one wave of CTAs (decode_stream_plan below); for the
+//     12-layer GPT-2 step of one sequence that is one CTA per (layer, head) streaming its whole
+//     context, so no cross-CTA merge is needed at all; batches of sequences use smaller CTAs
+//     (the mid and small shapes below), several per SM, each (sequence, head) pair whole;
 //   - warp 16 (one thread) issues cp.async.bulk copies of 128-key stages (16 KB of K + 16 KB of V,
 //     the slabs are contiguous) into a 4-stage shared-memory ring, tracked by mbarriers (128 KB in
 //     flight per SM: with more, the copies only queue longer in the memory system);
