@@ -243,14 +243,17 @@ def test_batch_step_b64_matches_reference(cuda, lib, ref_gpu, weights):
 
 
 @pytest.mark.parametrize("base", [500, 1000])
-def test_batch_step_long_context_b64_matches_reference(cuda, lib, ref_gpu, weights, base):
-    """configs[4] at long context: 64 sequences whose caches were filled by the reference's own
+@pytest.mark.parametrize("B", [64, 16, 8])
+def test_batch_step_long_context_b64_matches_reference(cuda, lib, ref_gpu, weights, base, B):
+    """configs[4] at long context: B sequences whose caches were filled by the reference's own
     prefill forward (gpt2_prefill_fill_cache, cuda/kvcache.cu:271-277) to positions around `base`
     take one batched step; every sequence's logits and appended K/V are compared with the
     reference's own decode step (gpt2_decode_step_cuda) from the same cache, and two sequences
-    also go through the single-sequence drop-in gpt2_decode_step_b200."""
+    also go through the single-sequence drop-in gpt2_decode_step_b200. B = 64 runs the step's
+    attention in the small-CTA shape, 16 in the mid shape and 8 one CTA per (sequence, head); the
+    last two as programmatic dependents that request the older K/V rows into L2 before their wait."""
     torch = cuda
-    B, MAXT, NV = 64, 1024, 8  # 8 distinct prompts (lengths base-4 .. base+3), each cache used 8 times
+    MAXT, NV = 1024, 8  # 8 distinct prompts (lengths base-4 .. base+3), each cache used B/8 times
     rng = np.random.default_rng(base)
     plen = [base - 4 + v for v in range(NV)]
     filled = torch.zeros(NV, G.N_LAYER, 2, G.N_HEAD, MAXT, 64, dtype=torch.float16, device="cuda")
