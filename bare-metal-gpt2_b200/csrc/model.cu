@@ -62,8 +62,20 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 }
 
 // LayerNorm of one fp16 row held as 3 floats per thread; writes fp16 out.
-__device__ __forceinline__ void ln_row(const float (&xv)[3], __half *out, const __half *g,
-                                       const __half *bta, float *red) {
+// This thread's 3 elements of the LayerNorm gain and bias. They are weights, which no kernel of the
+// step writes, so the LayerNorm kernels load them before their grid dependency wait: only the row
+// itself is then read after it.
+__device__ __forceinline__ void ln_params(const __half *g, const __half *bta, float (&gv)[3], float (&bv)[3]) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const int e = threadIdx.x + i * LN_THREADS;
+        gv[i] = __half2float(g[e]);
+        bv[i] = __half2float(bta[e]);
+    }
+}
+
+__device__ __forceinline__ void ln_row(const float (&xv)[3], __half *out, const float (&gv)[3],
+                                       const float (&bv)[3], float *red) {
     const float mean = block_sum(xv[0] + xv[1] + xv[2], red) / E;
     float d2 = 0.0f;
 #pragma unroll
@@ -73,7 +85,7 @@ __device__ __forceinline__ void ln_row(const float (&xv)[3], __half *out, const 
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         const int e = threadIdx.x + i * LN_THREADS;
-        out[e] = __float2half_rn((xv[i] - mean) * inv * __half2float(g[e]) + __half2float(bta[e]));
+        out[e] = __float2half_rn((xv[i] - mean) * inv * gv[i] + bv[i]);
     }
 }
 
@@ -83,6 +95,8 @@ __global__ void __launch_bounds__(LN_THREADS) k_embed_ln(__half *x, __half *ln, 
                                                          const __half *bta, const int *tok,
                                                          const int *pos, int maxT, unsigned *status) {
     __shared__ float red[LN_THREADS / 32];
+    float gv[3], bv[3];
+    ln_params(g, bta, gv, bv);
     grid_dependency_wait();
     grid_launch_dependents();
     const int b = blockIdx.x;
@@ -101,12 +115,14 @@ __global__ void __launch_bounds__(LN_THREADS) k_embed_ln(__half *x, __half *ln, 
         x[static_cast<long long>(b) * E + e] = h;
         xv[i] = __half2float(h);
     }
-    ln_row(xv, ln + static_cast<long long>(b) * E, g, bta, red);
+    ln_row(xv, ln + static_cast<long long>(b) * E, gv, bv, red);
 }
 
 __global__ void __launch_bounds__(LN_THREADS) k_layernorm(__half *ln, const __half *x,
                                                           const __half *g, const __half *bta) {
     __shared__ float red[LN_THREADS / 32];
+    float gv[3], bv[3];
+    ln_params(g, bta, gv, bv);
     grid_dependency_wait();
     grid_launch_dependents();
     const int b = blockIdx.x;
@@ -114,7 +130,7 @@ __global__ void __launch_bounds__(LN_THREADS) k_layernorm(__half *ln, const __ha
 #pragma unroll
     for (int i = 0; i < 3; ++i)
         xv[i] = __half2float(x[static_cast<long long>(b) * E + threadIdx.x + i * LN_THREADS]);
-    ln_row(xv, ln + static_cast<long long>(b) * E, g, bta, red);
+    ln_row(xv, ln + static_cast<long long>(b) * E, gv, bv, red);
 }
 
 // Best key of row b over the head's n_tiles tile keys (one block of 128 threads per row).
