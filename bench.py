@@ -515,8 +515,10 @@ def bench_model_decode(torch, lib, G, world, rank, seed, total_seqs=64, ctx=1023
     # (bound by HBM bandwidth) then overlaps the other's weight matmuls (bound by launch latency).
     # Measured, 64 sequences: 653 -> 606 ms for the whole generation; 32: 495 -> 482 ms; 16: 403 ->
     # 400 ms (not used). Each batch keeps >= 16 sequences (>= 192 (sequence, head) pairs), so its
-    # decode attention never splits a pair and the two never share the split workspace.
-    n_groups = 2 if B >= 32 else 1
+    # decode attention never splits a pair and the two never share the split workspace; the two
+    # batches have the same size, so their weight-matmul CTAs size their tensor-memory allocations
+    # alike (one size cannot oversubscribe an SM's tensor memory).
+    n_groups = 2 if B >= 32 and B % 2 == 0 else 1
     bounds = [B * g // n_groups for g in range(n_groups + 1)]
     handles, kv_arrays = [], []
     for g in range(n_groups):
